@@ -1,0 +1,177 @@
+/*
+ * sparse_attn_b200.h — C ABI of the B200 (sm_100a) block-sparse attention backend.
+ *
+ * Every entry point takes plain device pointers, sizes and strides (in elements),
+ * launches on the given CUDA stream, allocates nothing and never synchronises.
+ * Each returns 0 on success or a negative SA_ERR_* code; sa_last_error() then
+ * holds a one-line message for the calling host thread.
+ *
+ * The reference (rrroooyyywang/SparseAttentionInfer) has no native attention
+ * code; each entry point names the Python/Triton interface it replaces.
+ */
+#ifndef SPARSE_ATTN_B200_H
+#define SPARSE_ATTN_B200_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define SA_API __attribute__((visibility("default")))
+#else
+#define SA_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef void* sa_stream_t; /* a cudaStream_t (CUstream); NULL = legacy default stream */
+
+enum {
+  SA_OK = 0,
+  SA_ERR_INVALID = -1,     /* bad shape, stride, alignment or parameter          */
+  SA_ERR_UNSUPPORTED = -2, /* valid but unsupported (dtype, head_dim, device)    */
+  SA_ERR_CUDA = -3,        /* a CUDA runtime/driver call failed                   */
+  SA_ERR_TIMEOUT = -4,     /* a device-side bounded wait expired (see below)      */
+  SA_ERR_CSR = -5          /* CSR schedule failed host-side validation           */
+};
+
+/* BigBird layout of one KV group: (block_size, global, sliding, random), the
+ * tuple returned by bigbird_layout_from_topk / bigbird_layout_from_keep_ratio
+ * (sparse_attentions/patterns/bigbird_pattern.py:12-20, 338-363). */
+typedef struct {
+  int32_t block_size;
+  int32_t global_blocks;
+  int32_t sliding_blocks;
+  int32_t random_blocks;
+} sa_bigbird_layout;
+
+/* Pattern variants of sa_bigbird_offsets / sa_bigbird_pairs. */
+enum {
+  SA_BIGBIRD = 0,  /* BigBirdPattern / BigBirdKeepRatioPattern _get_block_pairs
+                      (bigbird_pattern.py:212-271, 533-583)                    */
+  SA_BIGBIRD2 = 1  /* BigBird2Pattern._get_block_pairs: last query-block row is
+                      every key block (bigbird_pattern.py:697-753)              */
+};
+
+/* Version string of the library build. */
+SA_API const char* sa_version(void);
+
+/* Message of the last failing call on this host thread ("" if none). */
+SA_API const char* sa_last_error(void);
+
+/* Read and clear the device-side error word that bounded waits set when they
+ * expire (SA_ERR_TIMEOUT) or that index checks set. Synchronises the device.
+ * *code receives 0 when no kernel reported an error. */
+SA_API int sa_device_error(int32_t* code);
+
+/* ---------------------------------------------------------------------------
+ * Pattern compiler (device side). Replaces the Python H x NQB loops of
+ * BigBirdPattern._get_block_pairs (bigbird_pattern.py:212-271),
+ * BigBirdKeepRatioPattern._get_block_pairs (:533-583) and
+ * BigBird2Pattern._get_block_pairs (:697-753), bit-exact with them:
+ * per head h and local query block qb the sorted union of global blocks
+ * [0,g), the window [max(0,qba-w+1), min(qba+1,NKB)) and the rotated random
+ * blocks of select_bigbird_random_block_ids (:23-41), qba = (T_k-T_q)/bs + qb.
+ *
+ * Two phases, because the reference's block_pairs width (max nnz over heads)
+ * is data dependent:
+ *   1. sa_bigbird_offsets writes offsets [H, NQB+1] (int32, per-head CSR
+ *      starting at 0), NQB = ceil(T_q/bs);
+ *   2. the caller reads max_h offsets[h, NQB], allocates pairs [H, max(1,that)]
+ *      and sa_bigbird_pairs fills it, zero padded like the reference.
+ * layouts is a HOST array of n_groups entries (n_groups divides n_heads; head h
+ * uses group h / (n_heads/n_groups)); only their g/w/r fields are used, the
+ * block size is `block_size` for every group (the reference uses
+ * _next_pow2_min16(layouts[0][0]) for all groups, bigbird_pattern.py:545).
+ * ------------------------------------------------------------------------- */
+SA_API int sa_bigbird_offsets(const sa_bigbird_layout* layouts, int32_t n_groups, int32_t n_heads,
+                       int32_t T_q, int32_t T_k, int32_t block_size, int32_t variant,
+                       int32_t* offsets, sa_stream_t stream);
+SA_API int sa_bigbird_pairs(const sa_bigbird_layout* layouts, int32_t n_groups, int32_t n_heads,
+                     int32_t T_q, int32_t T_k, int32_t block_size, int32_t variant,
+                     const int32_t* offsets, int32_t* pairs, int32_t max_pairs,
+                     sa_stream_t stream);
+
+/* Arbitrary retained-block masks. Replaces build_block_pairs_from_mask
+ * (sparse_attentions/patterns/base.py:36-89).
+ * sa_block_bitmap_from_token_mask: token mask [H, T_q, T_k] (bool/uint8,
+ * contiguous) -> block bitmap [H, NQB, NKB] (uint8 0/1): a block is kept when
+ * any token of it is kept (base.py:67-73).
+ * sa_bitmap_offsets / sa_bitmap_pairs: block bitmap -> CSR, same two-phase
+ * protocol as the BigBird compiler (base.py:75-89). */
+SA_API int sa_block_bitmap_from_token_mask(const uint8_t* token_mask, int32_t H, int32_t T_q,
+                                   int32_t T_k, int32_t block_size, uint8_t* bitmap,
+                                   sa_stream_t stream);
+SA_API int sa_bitmap_offsets(const uint8_t* bitmap, int32_t H, int32_t NQB, int32_t NKB,
+                      int32_t* offsets, sa_stream_t stream);
+SA_API int sa_bitmap_pairs(const uint8_t* bitmap, int32_t H, int32_t NQB, int32_t NKB,
+                    const int32_t* offsets, int32_t* pairs, int32_t max_pairs,
+                    sa_stream_t stream);
+
+/* Legacy padded schedule -> CSR. Replaces kv_block_list_to_pairs
+ * (sparse_attentions/patterns/base.py:92-133): kv_block_list [H, NQB, MAX_KV]
+ * int32 with -1 padding. Same two-phase protocol. */
+SA_API int sa_kvlist_offsets(const int32_t* kv_block_list, int32_t H, int32_t NQB, int32_t max_kv,
+                      int32_t* offsets, sa_stream_t stream);
+SA_API int sa_kvlist_pairs(const int32_t* kv_block_list, int32_t H, int32_t NQB, int32_t max_kv,
+                    const int32_t* offsets, int32_t* pairs, int32_t max_pairs,
+                    sa_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * Block-sparse attention forward (prefill / any T_q). Replaces
+ * universal_sparse_attn + _universal_sparse_attn_kernel
+ * (kernels/triton/universal_sparse_attn.py:45-238) behind
+ * TritonUniversalBackend.forward (sparse_attentions/attention/triton_universal_backend.py:47-66).
+ *
+ *   out[b,h,i,:] = sum_j softmax_j(scale * q[b,h,i]·k[b,kvh,j]) v[b,kvh,j]
+ * over keys j whose block j/bs is listed in CSR row (h, i/bs), with j <= i +
+ * (T_k - T_q) (causal, bottom-right aligned) and j < T_k. Rows with no valid
+ * key are written as 0 (universal_sparse_attn.py:150-153). kvh = h / (Hq/Hkv)
+ * (GQA without repeat_kv).
+ *
+ * q/out: [B, Hq, T_q, D] bf16, k/v: [B, Hkv, T_k, D] bf16, each with the given
+ * element strides for b, h and t (stride of d must be 1); strides and base
+ * addresses must be 16-byte aligned. D in {64, 128}. block_size a power of two
+ * in [16, 512]. pairs [Hq, pairs_stride] / offsets [Hq, NQB+1] int32 device
+ * arrays, NQB = ceil(T_q / block_size).
+ * Uses tcgen05 MMAs with TMEM accumulators and TMA tile loads; persistent grid.
+ * ------------------------------------------------------------------------- */
+typedef struct {
+  const void* q;
+  const void* k;
+  const void* v;
+  void* out;
+  const int32_t* pairs;
+  const int32_t* offsets;
+  int64_t q_strides[3];   /* b, h, t (elements) */
+  int64_t k_strides[3];
+  int64_t v_strides[3];
+  int64_t o_strides[3];
+  int32_t B, Hq, Hkv, T_q, T_k, D;
+  int32_t block_size;
+  int32_t pairs_stride;   /* row stride of pairs (elements) */
+  float scale;            /* softmax scale, usually 1/sqrt(D) */
+  int32_t num_sms;        /* persistent grid size; 0 = all SMs */
+} sa_attn_args;
+
+SA_API int sa_prefill_fwd(const sa_attn_args* args, sa_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * Split-KV sparse decode (T_q == 1). Replaces the decode use of
+ * universal_sparse_attn (Q_OFFSET = T_k, universal_sparse_attn.py:84-89),
+ * where the Triton kernel runs one 1-row query block per (b, h).
+ * One CTA per (b, kv head, split) serves the Hq/Hkv query heads of the group
+ * and reads the union of their CSR rows' key blocks once (the reference's
+ * random blocks differ per query head, bigbird_pattern.py:23-41).
+ * Scratch (caller-allocated, float32): partial_o [B, Hq, n_split, D] and
+ * partial_ml [B, Hq, n_split, 2]; a second kernel merges the splits into out.
+ * n_split in [1, 64]; Hq/Hkv <= 8; D in {64, 128}.
+ * ------------------------------------------------------------------------- */
+SA_API int sa_decode_fwd(const sa_attn_args* args, int32_t n_split, float* partial_o,
+                  float* partial_ml, sa_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SPARSE_ATTN_B200_H */

@@ -1,0 +1,116 @@
+"""ctypes binding of the C ABI declared in ``include/sparse_attn_b200.h``.
+
+The shared library is built in-tree (``_lib/libsa_b200.so``). There is no
+fallback: if the library is missing or fails to load, every entry point raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from pathlib import Path
+
+_PKG = Path(__file__).resolve().parent
+LIB_PATH = _PKG / "_lib" / "libsa_b200.so"
+
+# Every symbol include/sparse_attn_b200.h declares (checked by the CPU tests).
+EXPORTED = (
+    "sa_version",
+    "sa_last_error",
+    "sa_device_error",
+    "sa_bigbird_offsets",
+    "sa_bigbird_pairs",
+    "sa_block_bitmap_from_token_mask",
+    "sa_bitmap_offsets",
+    "sa_bitmap_pairs",
+    "sa_kvlist_offsets",
+    "sa_kvlist_pairs",
+    "sa_prefill_fwd",
+    "sa_decode_fwd",
+)
+
+SA_OK = 0
+SA_ERR_INVALID = -1
+SA_ERR_UNSUPPORTED = -2
+SA_ERR_CUDA = -3
+SA_ERR_TIMEOUT = -4
+SA_ERR_CSR = -5
+SA_BIGBIRD = 0
+SA_BIGBIRD2 = 1
+
+_c_i32 = ctypes.c_int32
+_c_i64 = ctypes.c_int64
+_c_p = ctypes.c_void_p
+
+
+class SaError(RuntimeError):
+    """Raised when a C ABI call returns a non-zero status."""
+
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"[sa error {code}] {msg}")
+        self.code = code
+
+
+class BigBirdLayout(ctypes.Structure):
+    _fields_ = [("block_size", _c_i32), ("global_blocks", _c_i32), ("sliding_blocks", _c_i32),
+                ("random_blocks", _c_i32)]
+
+
+class AttnArgs(ctypes.Structure):
+    _fields_ = [
+        ("q", _c_p), ("k", _c_p), ("v", _c_p), ("out", _c_p), ("pairs", _c_p), ("offsets", _c_p),
+        ("q_strides", _c_i64 * 3), ("k_strides", _c_i64 * 3), ("v_strides", _c_i64 * 3),
+        ("o_strides", _c_i64 * 3),
+        ("B", _c_i32), ("Hq", _c_i32), ("Hkv", _c_i32), ("T_q", _c_i32), ("T_k", _c_i32), ("D", _c_i32),
+        ("block_size", _c_i32), ("pairs_stride", _c_i32), ("scale", ctypes.c_float), ("num_sms", _c_i32),
+    ]
+
+
+_lib = None
+
+
+def load(path: str | os.PathLike | None = None) -> ctypes.CDLL:
+    """Load (once) and return the C-ABI library; raises if it is absent."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    p = Path(path) if path is not None else LIB_PATH
+    if not p.exists():
+        raise ImportError(
+            f"sparseattentioninfer_b200 C library not found at {p}; build it with "
+            "`python sparseattentioninfer_b200/_build.py` (no CPU fallback exists)")
+    lib = ctypes.CDLL(str(p))
+    lib.sa_version.restype = ctypes.c_char_p
+    lib.sa_last_error.restype = ctypes.c_char_p
+    lib.sa_device_error.argtypes = [ctypes.POINTER(_c_i32)]
+    lay = ctypes.POINTER(BigBirdLayout)
+    lib.sa_bigbird_offsets.argtypes = [lay, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_p, _c_p]
+    lib.sa_bigbird_pairs.argtypes = [lay, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_p, _c_p, _c_i32, _c_p]
+    lib.sa_block_bitmap_from_token_mask.argtypes = [_c_p, _c_i32, _c_i32, _c_i32, _c_i32, _c_p, _c_p]
+    lib.sa_bitmap_offsets.argtypes = [_c_p, _c_i32, _c_i32, _c_i32, _c_p, _c_p]
+    lib.sa_bitmap_pairs.argtypes = [_c_p, _c_i32, _c_i32, _c_i32, _c_p, _c_p, _c_i32, _c_p]
+    lib.sa_kvlist_offsets.argtypes = [_c_p, _c_i32, _c_i32, _c_i32, _c_p, _c_p]
+    lib.sa_kvlist_pairs.argtypes = [_c_p, _c_i32, _c_i32, _c_i32, _c_p, _c_p, _c_i32, _c_p]
+    lib.sa_prefill_fwd.argtypes = [ctypes.POINTER(AttnArgs), _c_p]
+    lib.sa_decode_fwd.argtypes = [ctypes.POINTER(AttnArgs), _c_i32, _c_p, _c_p, _c_p]
+    for name in EXPORTED:
+        if name not in ("sa_version", "sa_last_error"):
+            getattr(lib, name).restype = ctypes.c_int
+    _lib = lib
+    return lib
+
+
+def check(rc: int) -> None:
+    if rc != SA_OK:
+        msg = load().sa_last_error().decode(errors="replace")
+        raise SaError(rc, msg)
+
+
+def version() -> str:
+    return load().sa_version().decode()
+
+
+def device_error() -> int:
+    """Read and clear the device error word (synchronises the device)."""
+    code = _c_i32(0)
+    check(load().sa_device_error(ctypes.byref(code)))
+    return int(code.value)

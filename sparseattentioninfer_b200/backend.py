@@ -1,0 +1,114 @@
+"""Backend layer: the reference's AttentionBackend API served by the sm_100a kernels.
+
+``CudaSm100Backend`` is a drop-in for TritonUniversalBackend
+(sparse_attentions/attention/triton_universal_backend.py:24-103): same
+``forward(q, k, v, pattern) -> out`` and ``actual_backend`` property
+(sparse_attentions/attention/base.py:9-40), registered by name the way
+``_REGISTRY`` / ``get_backend`` do (sparse_attentions/attention/__init__.py:8-21).
+
+Unlike the reference there is no silent fallback: unsupported inputs raise,
+and ``actual_backend`` is always "cuda_sm100".
+"""
+from __future__ import annotations
+
+import math
+from abc import ABC, abstractmethod
+
+import torch
+
+from . import ops as _ops
+from .patterns import PatternMetadata
+
+
+class AttentionBackend(ABC):
+    """sparse_attentions/attention/base.py:9-40."""
+
+    @abstractmethod
+    def forward(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, pattern: PatternMetadata) -> torch.Tensor:
+        ...
+
+    @property
+    def actual_backend(self) -> str:
+        return type(self).__name__
+
+
+class CudaSm100Backend(AttentionBackend):
+    """Block-sparse attention on B200: tcgen05/TMEM prefill, split-KV decode.
+
+    Accepts q [B,H,T_q,D] and k/v with H or H/G heads (GQA without repeat_kv).
+    ``pattern.kind``:
+      * "mask" / "local" with a CSR (block_pairs, block_pair_offsets, block_size);
+        a pattern that only carries a token mask and a block_size is compiled
+        on the device first (build_block_pairs_from_mask semantics);
+      * "dense": full causal attention through a dense causal CSR (block 128) —
+        bottom-right aligned, so decode is correct (unlike dense_sdpa.py:24);
+      * "topk": data-dependent, not implemented by this backend (raises).
+    """
+
+    name = "cuda_sm100"
+
+    def __init__(self, dense_block_size: int = 128):
+        self.dense_block_size = dense_block_size
+        self._dense_cache: dict = {}
+        self._mask_cache: dict = {}
+        self._last = "cuda_sm100"
+
+    @property
+    def actual_backend(self) -> str:
+        return self._last
+
+    def _dense_csr(self, H: int, T_q: int, T_k: int, device) -> tuple[torch.Tensor, torch.Tensor, int]:
+        bs = self.dense_block_size
+        key = (H, T_q, T_k, str(device))
+        if key not in self._dense_cache:
+            nkb = math.ceil(T_k / bs)
+            pairs, offsets = _ops.compile_bigbird([(bs, 0, nkb, 0)], H, T_q, T_k, bs, device=device)
+            self._dense_cache[key] = (pairs, offsets, bs)
+        return self._dense_cache[key]
+
+    def forward(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, pattern: PatternMetadata) -> torch.Tensor:
+        if not q.is_cuda:
+            raise RuntimeError("cuda_sm100 backend needs CUDA tensors (no CPU fallback)")
+        H, T_q, T_k = q.size(1), q.size(2), k.size(2)
+        if pattern.kind == "dense":
+            pairs, offsets, bs = self._dense_csr(H, T_q, T_k, q.device)
+        elif pattern.kind in ("mask", "local"):
+            pairs, offsets, bs = pattern.block_pairs, pattern.block_pair_offsets, pattern.block_size
+            if pairs is None or offsets is None:
+                if pattern.mask is None or bs is None:
+                    raise ValueError("cuda_sm100 needs a block CSR (block_pairs/block_pair_offsets/block_size) "
+                                     "or a token mask plus block_size")
+                key = (id(pattern.mask), bs)
+                if key not in self._mask_cache:
+                    self._mask_cache = {key: _ops.compile_token_mask(pattern.mask, bs)}
+                pairs, offsets = self._mask_cache[key]
+            if bs is None:
+                raise ValueError("pattern.block_size is None")
+        else:
+            raise NotImplementedError(f"cuda_sm100 does not implement pattern kind {pattern.kind!r}")
+        self._last = "cuda_sm100"
+        return _ops.sparse_attn(q, k, v, pairs, offsets, int(bs))
+
+
+_REGISTRY: dict[str, type[AttentionBackend]] = {"cuda_sm100": CudaSm100Backend}
+
+
+def get_backend(name: str, **kwargs) -> AttentionBackend:
+    """sparse_attentions/attention/__init__.py:17-21."""
+    if name not in _REGISTRY:
+        raise ValueError(f"Unknown backend {name!r}. Available: {', '.join(sorted(_REGISTRY))}")
+    return _REGISTRY[name](**kwargs)
+
+
+def register_with_reference(registry: dict | None = None) -> dict:
+    """Insert "cuda_sm100" into the reference's backend registry.
+
+    With ``registry=None`` the registry of an importable
+    ``sparse_attentions.attention`` package is used (that package must be on
+    sys.path); its ``get_backend("cuda_sm100")`` then returns this backend.
+    """
+    if registry is None:
+        from sparse_attentions import attention as ref_attention  # type: ignore
+        registry = ref_attention._REGISTRY
+    registry["cuda_sm100"] = CudaSm100Backend
+    return registry
