@@ -1,0 +1,380 @@
+"""Benchmark of the block-sparse attention hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Headline (one JSON line on rank 0): "sparse-attn prefill TFLOP/s on retained
+blocks" on the arbitrary block-mask prefill configuration (B=4, H=32, S=8192,
+D=128, bf16, block 128, causal blocks kept with p=0.25, diagonal always) —
+FLOPs counted as 4*bs^2*D per retained (b, head, q-block, k-block) entry.
+A step is one prefill over the whole batch. With N GPUs each rank processes
+its own 32-head shard (heads sharded by KV group, no collective: weak scaling).
+
+Extra keys: roofline of the prefill kernel (vs measured dense bf16 peak),
+e2e (same metric through the public backend API with pinned host buffers and
+the H2D/D2H copies in the timed region), cpu_baseline (the CPU restatement of
+the reference's masked-dense algorithm on a bounded sample), decode (the
+split-KV decode kernel on the Qwen3-4B-shaped layer, HBM GB/s), clocks.
+
+--impl reference times the reference's own algorithm for this path on the
+host cores (MaskedSdpaBackend restated in oracle/, the reference being pure
+Python) on a bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+import torch  # noqa: E402
+
+METRIC = "sparse-attn prefill TFLOP/s on retained blocks"
+B, H, S, D, BS, P_KEEP = 4, 32, 8192, 128, 128, 0.25
+FALLBACK_PEAKS = {"bf16_tflops": 1590.0, "hbm_gbs": 6650.0}
+
+
+def load_peaks() -> tuple[dict, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        return json.loads(p.read_text()), "measured"
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+def traffic_from_profile(name: str):
+    """Per-launch DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) recorded
+    from an ncu capture in profiles/<name>; None when not captured yet."""
+    p = ROOT / "profiles" / name
+    if not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        if line.startswith("traffic_bytes_per_launch:"):
+            return float(line.split(":", 1)[1])
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle sampling during a timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+            time.sleep(0.25)
+        except Exception:  # noqa: BLE001
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:  # noqa: BLE001
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        if self.proc is None or not self.path or not os.path.exists(self.path):
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax = float(f[2])
+            except ValueError:
+                continue
+            for n, val in zip(names, f[5:9]):
+                if val.lower() == "active":
+                    reasons.add(n)
+        os.unlink(self.path)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def make_workload(rank: int, device):
+    """Config-2 shard of this rank: q/k/v N(0,1) bf16 (seed 1000+rank) and the
+    Bernoulli block bitmap (seed rank), CSR compiled on the device."""
+    from sparseattentioninfer_b200 import BlockMaskPattern, workloads as wl
+    q, k, v = wl.seeded_qkv(1000 + rank, B, H, H, S, S, D, device=device, dtype=torch.bfloat16)
+    nb = S // BS
+    bitmap = wl.bernoulli_block_bitmap(H, nb, nb, P_KEEP, seed=rank, device=device)
+    md = BlockMaskPattern(bitmap, BS).build(q, k)
+    nnz = int(md.block_pair_offsets[:, -1].long().sum().item())
+    flops = 4 * BS * BS * D * nnz * B
+    return q, k, v, md, bitmap, flops
+
+
+def cpu_sample(bitmap_cpu: torch.Tensor, seconds: float, max_slices: int, threads: int):
+    """Time the CPU restatement of MaskedSdpaBackend (masked_sdpa.py:23-68) on
+    (b, h) slices of the workload until `seconds` elapsed; returns
+    (TFLOP/s on retained blocks, slices done, wall seconds)."""
+    import oracle
+    from sparseattentioninfer_b200 import workloads as wl
+    torch.set_num_threads(threads)
+    q, k, v = wl.seeded_qkv(1000, 1, 1, 1, S, S, D, dtype=torch.bfloat16)
+    q, k, v = q.float(), k.float(), v.float()
+    flops = done = 0
+    t0 = time.perf_counter()
+    for h in range(max_slices):
+        hh = h % H
+        bm = bitmap_cpu[hh].bool()
+        keep_fn = (lambda _h, r0, r1, bm=bm: bm[torch.arange(r0, r1) // BS][:, torch.arange(S) // BS])
+        oracle.masked_sdpa_chunked(q, k, v, keep_fn, row_chunk=1024)
+        flops += 4 * BS * BS * D * int(bm.sum())
+        done += 1
+        if time.perf_counter() - t0 > seconds:
+            break
+    wall = time.perf_counter() - t0
+    return flops / wall / 1e12, done, wall
+
+
+def run_reference(args) -> None:
+    world, rank, _ = dist_env()
+    if rank != 0:
+        return
+    from sparseattentioninfer_b200 import workloads as wl
+    threads = os.cpu_count() or 1
+    nb = S // BS
+    bitmap = wl.bernoulli_block_bitmap(H, nb, nb, P_KEEP, seed=0)
+    per_step_slices = 2
+    times, rates = [], []
+    for i in range(args.warmup + args.steps):
+        rate, done, wall = cpu_sample(bitmap, 1e9, per_step_slices, threads)
+        if i >= args.warmup:
+            times.append(wall)
+            rates.append(rate)
+    value = statistics.mean(rates)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * statistics.mean(times),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "arbitrary_block_mask_b4_h32_s8192_d128_bs128_p0.25",
+                   "sample": f"{per_step_slices} (b,h) slices per step of the B=4,H=32 workload"},
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+                         "sample": f"{per_step_slices} (b,h) slices of S=8192 per step, masked-dense fp32"},
+        "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def time_decode(device) -> dict:
+    """Split-KV decode on the Qwen3-4B-shaped attention layer: B=32, Hq=32,
+    Hkv=8, D=128, T_k=32768 bf16 cache, BigBird (64, 2, 4, 2). Algorithmic bytes
+    = union of retained KV blocks per (b, kv-group) x 64 x 128 x 2 (K,V) x 2 B
+    + q/out."""
+    from sparseattentioninfer_b200 import BigBirdKeepRatioPattern, ops, workloads as wl
+    Bd, Hq, Hkv, T = 32, 32, 8, 32768
+    q, k, v = wl.seeded_qkv(7, Bd, Hq, Hkv, 1, T, D, device=device, dtype=torch.bfloat16)
+    md = BigBirdKeepRatioPattern(layouts=[(64, 2, 4, 2)], n_heads=Hq).build(q, k)
+    pairs, offs = md.block_pairs, md.block_pair_offsets
+    # union size per kv group (same for every batch row)
+    rows = []
+    for h in range(Hq):
+        o0, o1 = int(offs[h, 0]), int(offs[h, 1])
+        rows.append(set(int(x) for x in pairs[h, o0:o1].tolist()))
+    nblk = 0
+    for gi in range(Hkv):
+        u = set().union(*rows[gi * 4:(gi + 1) * 4])
+        nblk += sum(1 for kb in u if kb * 64 < T)
+    alg_bytes = Bd * nblk * 64 * D * 2 * 2 + 2 * Bd * Hq * D * 2
+    ns = ops.default_n_split(q, k)
+    ws = (torch.empty(Bd * Hq * ns * D, device=device), torch.empty(Bd * Hq * ns * 2, device=device))
+    out = torch.empty_like(q)
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=device)
+    for _ in range(5):
+        ops.decode_fwd(q, k, v, pairs, offs, 64, n_split=ns, out=out, workspace=ws)
+    ts = []
+    for _ in range(30):
+        flush.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        ops.decode_fwd(q, k, v, pairs, offs, 64, n_split=ns, out=out, workspace=ws)
+        e1.record()
+        torch.cuda.synchronize()
+        ts.append(e0.elapsed_time(e1) / 1e3)
+    t = statistics.median(ts)
+    return {"workload": "qwen3_4b_layer_decode_b32_h32kv8_t32768_bigbird64_2_4_2", "us_per_step": t * 1e6,
+            "alg_bytes": alg_bytes, "achieved_gbs": alg_bytes / t / 1e9, "n_split": ns,
+            "note": "2 launches per step (split + combine); L2 flushed between steps"}
+
+
+def run_ours(args) -> None:
+    world, rank, local = dist_env()
+    if world > 1:
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    import sparseattentioninfer_b200 as sa
+    from sparseattentioninfer_b200 import ops
+
+    peaks, peak_kind = load_peaks()
+    q, k, v, md, bitmap, flops = make_workload(rank, device)
+    pairs, offs = md.block_pairs, md.block_pair_offsets
+    out = torch.empty_like(q)
+    stream = torch.cuda.current_stream(device)
+
+    def step():
+        ops.prefill_fwd(q, k, v, pairs, offs, BS, out=out)
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize()
+
+    with ClockSampler(local) as cs:
+        # per-launch kernel timing (dominant kernel) with events on the launching stream
+        per = []
+        for _ in range(min(args.steps, 50)):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            step()
+            e1.record(stream)
+            e1.synchronize()
+            per.append(e0.elapsed_time(e1) / 1e3)
+        # whole-job throughput: K back-to-back steps (inputs 805 MB >> 126 MB L2)
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            step()
+        e1.record(stream)
+        barrier()
+        elapsed = e0.elapsed_time(e1) / 1e3
+        # e2e through the public backend API with pinned host buffers
+        backend = sa.get_backend("cuda_sm100")
+        hq, hk, hv = (t.cpu().pin_memory() for t in (q, k, v))
+        hout = torch.empty(q.shape, dtype=q.dtype).pin_memory()
+        e2e_steps = max(3, min(args.steps // 20, 20))
+
+        def e2e_step():
+            dq = hq.to(device, non_blocking=True)
+            dk = hk.to(device, non_blocking=True)
+            dv = hv.to(device, non_blocking=True)
+            o = backend.forward(dq, dk, dv, md)
+            hout.copy_(o, non_blocking=True)
+
+        e2e_step()
+        barrier()
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f0.record(stream)
+        for _ in range(e2e_steps):
+            e2e_step()
+        f1.record(stream)
+        barrier()
+        e2e_elapsed = f0.elapsed_time(f1) / 1e3
+    clocks = cs.summary()
+
+    t_launch = statistics.median(per)
+    if world > 1:
+        import torch.distributed as dist
+        tt = torch.tensor([elapsed, e2e_elapsed, t_launch], device=device)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        elapsed, e2e_elapsed, t_launch = (float(x) for x in tt.tolist())
+        ft = torch.tensor([float(flops)], device=device, dtype=torch.float64)
+        dist.all_reduce(ft)
+        total_flops = float(ft.item())
+    else:
+        total_flops = float(flops)
+
+    if rank != 0:
+        if world > 1:
+            torch.distributed.destroy_process_group()
+        return
+
+    value = total_flops * args.steps / elapsed / 1e12
+    achieved = flops / t_launch / 1e12
+    peak = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
+    in_bytes = 3 * q.numel() * 2
+    line = {
+        "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": elapsed / args.steps * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "arbitrary_block_mask_b4_h32_s8192_d128_bs128_p0.25",
+                   "per_rank": f"B={B} H={H} S={S} D={D} (rank r owns heads [32r, 32r+32))",
+                   "retained_blocks_per_rank": flops // (4 * BS * BS * D * B),
+                   "l2": "inputs 805 MB per rank > 126 MB L2; no flush"},
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                     "frac": achieved / peak, "peak_kind": f"{peak_kind} bf16 dense (burst)",
+                     "traffic": traffic_from_profile("prefill_cfg2_ncu.txt"),
+                     "kernel": "sa::prefill_kernel<128,128>", "launch_ms": t_launch * 1e3},
+        "e2e": {"value": total_flops * e2e_steps / e2e_elapsed / 1e12, "unit": "TFLOP/s",
+                "h2d_bytes_per_step": in_bytes, "d2h_bytes_per_step": q.numel() * 2,
+                "ms_per_step": e2e_elapsed / e2e_steps * 1e3,
+                "path": "CudaSm100Backend.forward (C ABI) with pinned host q/k/v/out"},
+        "gpu_launches": args.steps,
+        "clocks": clocks,
+    }
+    try:
+        line["decode"] = time_decode(device)
+        hb = float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))
+        line["decode"]["roofline_frac"] = line["decode"]["achieved_gbs"] / hb
+        line["decode"]["peak_gbs"] = hb
+    except Exception as e:  # noqa: BLE001
+        line["decode"] = {"error": repr(e)}
+    if world == 1 and not args.no_cpu_baseline:
+        threads = os.cpu_count() or 1
+        rate, done, wall = cpu_sample(bitmap.cpu(), args.cpu_seconds, 64, threads)
+        line["cpu_baseline"] = {"value": rate, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+                                "sample": f"{done} (b,h) slices of S=8192 (masked-dense fp32, reference "
+                                          f"algorithm restated), {wall:.1f} s"}
+    print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.destroy_process_group()
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=300)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -14,7 +14,7 @@ DEV = "cuda:0"
 
 
 def _pattern_for(meta):
-    kind, H = meta["kind"], meta["H"]
+    kind, H = meta["kind"], meta.get("H")
     kw = dict(exact_width=True, build_kv_block_list=True)
     if kind == "bigbird_topk":
         return sa.BigBirdPattern(top_k=meta["top_k"], n_heads=H, **kw)
