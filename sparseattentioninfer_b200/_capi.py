@@ -69,11 +69,12 @@ _lib = None
 
 
 def load(path: str | os.PathLike | None = None) -> ctypes.CDLL:
-    """Load (once) and return the C-ABI library; raises if it is absent."""
+    """Load (once) and return the C-ABI library; raises if it is absent.
+    ``SA_LIBRARY`` overrides the path (e.g. an instrumented debug build)."""
     global _lib
     if _lib is not None:
         return _lib
-    p = Path(path) if path is not None else LIB_PATH
+    p = Path(path) if path is not None else Path(os.environ.get("SA_LIBRARY", LIB_PATH))
     if not p.exists():
         raise ImportError(
             f"sparseattentioninfer_b200 C library not found at {p}; build it with "

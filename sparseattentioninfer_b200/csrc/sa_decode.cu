@@ -5,21 +5,28 @@
 // which spends a 1-row query block per (b, q-head) and re-reads K/V per head.
 // Here one CTA serves a (b, kv-head, split): it reads each retained KV block of
 // the group once for all Hq/Hkv query heads. The reference draws different
-// random blocks per query head (bigbird_pattern.py:23-41), so the CTA walks the
-// sorted union of the group's CSR rows with a per-head membership mask.
-// Memory path: 128-bit loads, D/8 lanes per key row, 4 rows in flight per lane
-// for K and for V; statistics in fp32 (log2 domain). A second kernel merges the
-// splits (log-sum-exp) and writes bf16.
+// random blocks per query head (bigbird_pattern.py:23-41), so the CTA first
+// builds the sorted union of the group's CSR rows in shared memory (a per-block
+// head bitmask, filled in parallel and compacted), then takes its contiguous
+// share of the union.
+// Memory path: a ring of kDecStages stages of up to 64 keys of K and V, filled
+// by untiled bulk copies (cp.async.bulk, mbarrier completion) issued by one
+// thread, so a whole stage is in flight per instruction; four warps consume
+// each stage from shared memory (D/8 lanes per key row, 16-byte reads).
+// Statistics in fp32 (log2 domain). A second kernel merges the splits
+// (log-sum-exp) and writes bf16.
 #include <cstring>
 
 #include "sa_common.cuh"
 
 namespace sa {
 
-constexpr int kDecThreads = 256;
+constexpr int kDecThreads = 128;
 constexpr int kDecWarps = kDecThreads / 32;
-constexpr int kMaxUnion = 2048;
-constexpr int kUnroll = 4;
+constexpr int kDecStages = 3;
+constexpr int kDecChunk = 64;        // keys per stage
+constexpr int kMaxUnion = 2048;      // union entries per (b, kv head)
+constexpr int kMaxNkbWords = 2048;   // membership bytes packed 4 per word: NKB <= 8192
 
 struct DecodeParams {
   const __nv_bfloat16* q;
@@ -36,6 +43,12 @@ struct DecodeParams {
   int32_t* err;
 };
 
+template <int D>
+struct DecodeCfg {
+  static constexpr int kStageBytes = kDecChunk * D * 2;  // K (or V) of one stage
+  static constexpr int kSmemBytes = 2 * kDecStages * kStageBytes + 128;
+};
+
 __device__ __forceinline__ void bf16x8_to_f32(const uint4 u, float (&f)[8]) {
   const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
 #pragma unroll
@@ -46,63 +59,145 @@ __device__ __forceinline__ void bf16x8_to_f32(const uint4 u, float (&f)[8]) {
   }
 }
 
+// Issue the bulk copies of one stage (rows [key0, key0+rows) of K and V).
+template <int D>
+__device__ __forceinline__ void issue_stage(const DecodeParams& p, int b, int kvh, int key0, int rows,
+                                            uint32_t sk, uint32_t sv, uint32_t bar) {
+  constexpr uint32_t kRow = D * 2;
+  if (rows <= 0) {
+    mbar_arrive(bar);
+    return;
+  }
+  mbar_arrive_expect_tx(bar, 2u * rows * kRow);
+  const __nv_bfloat16* kp = p.k + (int64_t)b * p.k_sb + (int64_t)kvh * p.k_sh + (int64_t)key0 * p.k_st;
+  const __nv_bfloat16* vp = p.v + (int64_t)b * p.v_sb + (int64_t)kvh * p.v_sh + (int64_t)key0 * p.v_st;
+  if (p.k_st == D) {
+    bulk_load(sk, kp, rows * kRow, bar);
+  } else {
+    for (int r = 0; r < rows; ++r) bulk_load(sk + r * kRow, kp + (int64_t)r * p.k_st, kRow, bar);
+  }
+  if (p.v_st == D) {
+    bulk_load(sv, vp, rows * kRow, bar);
+  } else {
+    for (int r = 0; r < rows; ++r) bulk_load(sv + r * kRow, vp + (int64_t)r * p.v_st, kRow, bar);
+  }
+}
+
 template <int D, int G>
 __global__ void __launch_bounds__(kDecThreads) decode_split_kernel(const DecodeParams p) {
+  using Cfg = DecodeCfg<D>;
   constexpr int LPK = D / 8;          // lanes per key row (16 B each)
   constexpr int KPW = 32 / LPK;       // key rows per warp instruction
+  constexpr int KPWARP = kDecChunk / kDecWarps;  // keys of a stage per warp
+  constexpr int IT = KPWARP / KPW;    // warp instructions per stage
   __shared__ int s_kb[kMaxUnion];
-  __shared__ uint8_t s_mask[kMaxUnion];
-  __shared__ int s_n;
+  __shared__ uint8_t s_hm[kMaxUnion];
+  __shared__ int s_warp_cnt[kDecWarps + 1];
+  __shared__ __align__(8) uint64_t bar_full[kDecStages], bar_empty[kDecStages];
   __shared__ float s_m[kDecWarps][G], s_l[kDecWarps][G];
-  __shared__ float s_o[kDecWarps][G][D];
+  __shared__ int abort_flag;
+  extern __shared__ __align__(128) uint8_t dsmem[];
+  const uint32_t sbase = (smem_u32(dsmem) + 127u) & ~127u;
+  // The stage ring is free before the first copy and after the drain: it holds
+  // the membership words first and the per-warp partial outputs last.
+  uint32_t* s_memb = reinterpret_cast<uint32_t*>(dsmem + (sbase - smem_u32(dsmem)));
+  float(*s_o)[G][D] = reinterpret_cast<float(*)[G][D]>(dsmem + (sbase - smem_u32(dsmem)));
+  static_assert(kMaxNkbWords * 4 <= 2 * kDecStages * DecodeCfg<D>::kStageBytes, "ring too small");
+  static_assert(kDecWarps * G * D * 4 <= 2 * kDecStages * DecodeCfg<D>::kStageBytes, "ring too small");
 
   const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int h0 = kvh * G;
+  const int nkb = (p.T_k + p.bs - 1) / p.bs;
+  const int nwords = (nkb + 3) >> 2;
 
-  // Union of the G query heads' rows (single thread; rows are short).
-  if (threadIdx.x == 0) {
-    int ptr[G], end[G];
-    const int32_t* prs[G];
-#pragma unroll
-    for (int j = 0; j < G; ++j) {
-      const int32_t* off = p.offsets + (int64_t)(h0 + j) * 2;
-      ptr[j] = off[0];
-      end[j] = off[1];
-      prs[j] = p.pairs + (int64_t)(h0 + j) * p.pairs_stride;
+  if (tid == 0) {
+    for (int i = 0; i < kDecStages; ++i) {
+      mbar_init(smem_u32(&bar_full[i]), 1);
+      mbar_init(smem_u32(&bar_empty[i]), kDecWarps);
     }
-    int n = 0;
-    while (true) {
-      int best = 0x7fffffff;
-#pragma unroll
-      for (int j = 0; j < G; ++j)
-        if (ptr[j] < end[j]) best = min(best, prs[j][ptr[j]]);
-      if (best == 0x7fffffff) break;
-      uint32_t m = 0;
-#pragma unroll
-      for (int j = 0; j < G; ++j)
-        if (ptr[j] < end[j] && prs[j][ptr[j]] == best) {
-          m |= 1u << j;
-          ++ptr[j];
-        }
-      if (n >= kMaxUnion) {
-        record_error(p.err, SA_DEV_ERR_INDEX);
-        break;
-      }
-      if (best < 0) m = 0;  // malformed index: contributes nothing
-      s_kb[n] = best < 0 ? 0 : best;
-      s_mask[n] = (uint8_t)m;
-      ++n;
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (nwords > kMaxNkbWords) {  // block-uniform
+    if (tid == 0) record_error(p.err, SA_DEV_ERR_INDEX);
+    return;
+  }
+  for (int i = tid; i < nwords; i += kDecThreads) s_memb[i] = 0u;
+  __syncthreads();
+  // Membership bytes: bit j of byte kb = query head h0+j lists block kb.
+#pragma unroll 1
+  for (int j = 0; j < G; ++j) {
+    const int32_t* off = p.offsets + (int64_t)(h0 + j) * 2;
+    const int r0 = __ldg(off), r1 = __ldg(off + 1);
+    const int32_t* row = p.pairs + (int64_t)(h0 + j) * p.pairs_stride;
+    for (int i = r0 + tid; i < r1; i += kDecThreads) {
+      const int kb = __ldg(row + i);
+      if (kb >= 0 && kb < nkb) atomicOr(&s_memb[kb >> 2], (1u << j) << ((kb & 3) * 8));
     }
-    s_n = n;
   }
   __syncthreads();
-  const int U = s_n;
+  // Compact to the sorted union: thread t owns words [t*per, (t+1)*per).
+  const int per = (nwords + kDecThreads - 1) / kDecThreads;
+  int cnt = 0;
+  for (int w = tid * per; w < min(nwords, (tid + 1) * per); ++w) {
+    const uint32_t x = s_memb[w];
+    cnt += ((x & 0xffu) != 0) + ((x & 0xff00u) != 0) + ((x & 0xff0000u) != 0) + ((x >> 24) != 0);
+  }
+  int incl = cnt;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  if (lane == 31) s_warp_cnt[warp] = incl;
+  __syncthreads();
+  if (tid == 0) {
+    int acc = 0;
+    for (int w = 0; w < kDecWarps; ++w) {
+      const int c = s_warp_cnt[w];
+      s_warp_cnt[w] = acc;
+      acc += c;
+    }
+    s_warp_cnt[kDecWarps] = acc;
+  }
+  __syncthreads();
+  {
+    int pos = s_warp_cnt[warp] + incl - cnt;
+    for (int w = tid * per; w < min(nwords, (tid + 1) * per); ++w) {
+      const uint32_t x = s_memb[w];
+#pragma unroll
+      for (int by = 0; by < 4; ++by) {
+        const uint32_t m = (x >> (8 * by)) & 0xffu;
+        if (m && pos < kMaxUnion) {
+          s_kb[pos] = w * 4 + by;
+          s_hm[pos] = (uint8_t)m;
+          ++pos;
+        }
+      }
+    }
+  }
+  __syncthreads();  // membership words no longer needed: the ring may be filled
+  const int U = min(s_warp_cnt[kDecWarps], kMaxUnion);
+  if (tid == 0 && s_warp_cnt[kDecWarps] > kMaxUnion) record_error(p.err, SA_DEV_ERR_INDEX);
   const int e_begin = (int)(((int64_t)U * split) / p.n_split);
   const int e_end = (int)(((int64_t)U * (split + 1)) / p.n_split);
-  const int nkeys = (e_end - e_begin) * p.bs;
+  const int chk = min(p.bs, kDecChunk);      // keys per stage
+  const int nsub = p.bs > kDecChunk ? p.bs / kDecChunk : 1;
+  const int nst = (e_end - e_begin) * nsub;  // stages of this split
 
-  // q slice of this lane, pre-scaled into the log2 domain.
+  auto stage_key0 = [&](int i) { return s_kb[e_begin + i / nsub] * p.bs + (i % nsub) * chk; };
+  auto stage_rows = [&](int i) { return max(0, min(chk, p.T_k - stage_key0(i))); };
+  auto sK = [&](int slot) { return sbase + slot * 2 * Cfg::kStageBytes; };
+  auto sV = [&](int slot) { return sbase + slot * 2 * Cfg::kStageBytes + Cfg::kStageBytes; };
+
+  if (tid == 0) {
+    // generic-proxy writes (membership words) precede async-proxy writes here
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    for (int i = 0; i < min(nst, kDecStages); ++i)
+      issue_stage<D>(p, b, kvh, stage_key0(i), stage_rows(i), sK(i), sV(i), smem_u32(&bar_full[i]));
+  }
+
   const int dsl = (lane % LPK) * 8;
   const int kr = lane / LPK;
   float qf[G][8];
@@ -121,36 +216,23 @@ __global__ void __launch_bounds__(kDecThreads) decode_split_kernel(const DecodeP
 #pragma unroll
     for (int e = 0; e < 8; ++e) o[j][e] = 0.f;
   }
-  const __nv_bfloat16* kbase = p.k + (int64_t)b * p.k_sb + (int64_t)kvh * p.k_sh + dsl;
-  const __nv_bfloat16* vbase = p.v + (int64_t)b * p.v_sb + (int64_t)kvh * p.v_sh + dsl;
-
-  constexpr int kBatch = kUnroll * KPW;  // keys per warp batch
-  for (int f0 = warp * kBatch; f0 < nkeys; f0 += kDecWarps * kBatch) {
-    uint4 ku[kUnroll], vu[kUnroll];
-    int key[kUnroll];
-    uint32_t hm[kUnroll];
+  volatile int* abort_v = &abort_flag;
+  bool ok = true;
+  for (int i = 0; i < nst; ++i) {
+    const int slot = i % kDecStages;
+    ok = mbar_wait(smem_u32(&bar_full[slot]), (i / kDecStages) & 1, abort_v, p.err);
+    if (!__all_sync(0xffffffffu, ok)) break;
+    const int rows = stage_rows(i);
+    const uint32_t hm = s_hm[e_begin + i / nsub];
+    const uint8_t* kst = dsmem + (sK(slot) - smem_u32(dsmem));
+    const uint8_t* vst = dsmem + (sV(slot) - smem_u32(dsmem));
+    float x[IT][G];
 #pragma unroll
-    for (int u = 0; u < kUnroll; ++u) {
-      const int f = f0 + u * KPW + kr;
-      key[u] = -1;
-      hm[u] = 0;
-      if (f < nkeys) {
-        const int e = e_begin + f / p.bs;
-        const int kk = s_kb[e] * p.bs + (f % p.bs);
-        if (kk < p.T_k) {
-          key[u] = kk;
-          hm[u] = s_mask[e];
-        }
-      }
-      const int kload = key[u] < 0 ? 0 : key[u];
-      ku[u] = __ldg(reinterpret_cast<const uint4*>(kbase + (int64_t)kload * p.k_st));
-      vu[u] = __ldg(reinterpret_cast<const uint4*>(vbase + (int64_t)kload * p.v_st));
-    }
-    float x[kUnroll][G];
-#pragma unroll
-    for (int u = 0; u < kUnroll; ++u) {
+    for (int it = 0; it < IT; ++it) {
+      const int r = warp * KPWARP + it * KPW + kr;
       float kf[8];
-      bf16x8_to_f32(ku[u], kf);
+      bf16x8_to_f32(*reinterpret_cast<const uint4*>(kst + r * D * 2 + dsl * 2), kf);
+      const bool valid = r < rows;
 #pragma unroll
       for (int j = 0; j < G; ++j) {
         float d = 0.f;
@@ -158,31 +240,56 @@ __global__ void __launch_bounds__(kDecThreads) decode_split_kernel(const DecodeP
         for (int e = 0; e < 8; ++e) d = fmaf(qf[j][e], kf[e], d);
 #pragma unroll
         for (int off = LPK / 2; off >= 1; off >>= 1) d += __shfl_xor_sync(0xffffffffu, d, off);
-        x[u][j] = (key[u] >= 0 && ((hm[u] >> j) & 1u)) ? d : -INFINITY;
+        x[it][j] = (valid && ((hm >> j) & 1u)) ? d : -INFINITY;
       }
     }
 #pragma unroll
     for (int j = 0; j < G; ++j) {
       float mb = m[j];
 #pragma unroll
-      for (int u = 0; u < kUnroll; ++u) mb = fmaxf(mb, x[u][j]);
+      for (int it = 0; it < IT; ++it) mb = fmaxf(mb, x[it][j]);
       const float mu = mb == -INFINITY ? 0.f : mb;
-      const float alpha = ex2(m[j] - mu);  // 0 when m = -inf
+      const float alpha = ex2(m[j] - mu);
       l[j] *= alpha;
 #pragma unroll
       for (int e = 0; e < 8; ++e) o[j][e] *= alpha;
       m[j] = mb;
+    }
 #pragma unroll
-      for (int u = 0; u < kUnroll; ++u) {
-        const float pj = ex2(x[u][j] - mu);
+    for (int it = 0; it < IT; ++it) {
+      const int r = warp * KPWARP + it * KPW + kr;
+      float vf[8];
+      bf16x8_to_f32(*reinterpret_cast<const uint4*>(vst + r * D * 2 + dsl * 2), vf);
+      if (r >= rows) {  // rows past T_k were not copied this time: never multiply them
+#pragma unroll
+        for (int e = 0; e < 8; ++e) vf[e] = 0.f;
+      }
+#pragma unroll
+      for (int j = 0; j < G; ++j) {
+        const float mu = m[j] == -INFINITY ? 0.f : m[j];
+        const float pj = ex2(x[it][j] - mu);
         l[j] += pj;
-        float vf[8];
-        bf16x8_to_f32(vu[u], vf);
 #pragma unroll
         for (int e = 0; e < 8; ++e) o[j][e] = fmaf(pj, vf[e], o[j][e]);
       }
     }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(smem_u32(&bar_empty[slot]));
+    if (tid == 0 && i + kDecStages < nst) {
+      // refill this slot once every warp has consumed it
+      ok = mbar_wait(smem_u32(&bar_empty[slot]), (i / kDecStages) & 1, abort_v, p.err);
+      if (ok)
+        issue_stage<D>(p, b, kvh, stage_key0(i + kDecStages), stage_rows(i + kDecStages), sK(slot), sV(slot),
+                       smem_u32(&bar_full[slot]));
+    }
   }
+  // Drain (bounded) copies still in flight before the ring is reused or the CTA exits.
+  if (tid == 0) {
+    int zero = 0;
+    for (int i = max(0, nst - kDecStages); i < nst; ++i)
+      mbar_wait(smem_u32(&bar_full[i % kDecStages]), (i / kDecStages) & 1, &zero, nullptr);
+  }
+  __syncthreads();  // ring idle: reuse it for the per-warp partials
   // Merge the KPW key rows of a warp (lanes with equal d-slice).
 #pragma unroll
   for (int off = LPK; off < 32; off <<= 1) {
@@ -215,7 +322,7 @@ __global__ void __launch_bounds__(kDecThreads) decode_split_kernel(const DecodeP
   }
   __syncthreads();
   // Merge the warps: one thread per (head, d).
-  for (int idx = threadIdx.x; idx < G * D; idx += kDecThreads) {
+  for (int idx = tid; idx < G * D; idx += kDecThreads) {
     const int j = idx / D, d = idx % D;
     float mx = -INFINITY;
 #pragma unroll
@@ -228,11 +335,11 @@ __global__ void __launch_bounds__(kDecThreads) decode_split_kernel(const DecodeP
       lsum += s_l[w][j] * c;
       acc += s_o[w][j][d] * c;
     }
-    const int64_t row = ((int64_t)b * p.Hq + h0 + j) * p.n_split + split;
-    p.part_o[row * D + d] = acc;
+    const int64_t rowi = ((int64_t)b * p.Hq + h0 + j) * p.n_split + split;
+    p.part_o[rowi * D + d] = acc;
     if (d == 0) {
-      p.part_ml[row * 2] = mx;
-      p.part_ml[row * 2 + 1] = lsum;
+      p.part_ml[rowi * 2] = mx;
+      p.part_ml[rowi * 2 + 1] = lsum;
     }
   }
 }
@@ -262,7 +369,9 @@ __global__ void __launch_bounds__(D) decode_combine_kernel(const float* __restri
 template <int D, int G>
 static int launch_decode(const DecodeParams& prm, const sa_attn_args* a, cudaStream_t stream) {
   dim3 grid(prm.n_split, prm.Hkv, prm.B);
-  decode_split_kernel<D, G><<<grid, kDecThreads, 0, stream>>>(prm);
+  SA_CHECK_CUDA(cudaFuncSetAttribute(decode_split_kernel<D, G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     DecodeCfg<D>::kSmemBytes));
+  decode_split_kernel<D, G><<<grid, kDecThreads, DecodeCfg<D>::kSmemBytes, stream>>>(prm);
   SA_CHECK_CUDA(cudaGetLastError());
   decode_combine_kernel<D><<<prm.B * prm.Hq, D, 0, stream>>>(
       prm.part_o, prm.part_ml, reinterpret_cast<__nv_bfloat16*>(a->out), a->o_strides[0],

@@ -25,11 +25,25 @@
 // Tiles are visited heaviest-first (last query tiles first) with a static
 // stride over the persistent grid.
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 
 #include "sa_common.cuh"
 
 namespace sa {
+
+#ifdef SA_PHASE_TRACE
+// Debug-only phase timestamps (clock64) of CTA 0: 16 slots per chunk step.
+__device__ unsigned long long g_sa_trace[16 * 512];
+#define SA_TRACE(step, slot)                                                           \
+  do {                                                                                 \
+    if (blockIdx.x == 0 && (step) < 512) g_sa_trace[(step) * 16 + (slot)] = clock64(); \
+  } while (0)
+#else
+#define SA_TRACE(step, slot) \
+  do {                       \
+  } while (0)
+#endif
 
 struct PrefillParams {
   CUtensorMap tm_q;
@@ -45,33 +59,55 @@ struct PrefillParams {
   int32_t* err;
 };
 
-constexpr int kThreads = 192;
+constexpr int kThreads = 192;  // warp 0 producer, warp 1 MMA issuer, warps 2..5 softmax
 constexpr int kTileM = 128;
 constexpr int kMaxSeg = 8;  // 128 / 16
+// Chunk metadata ring. The producer runs at most kKStages chunks ahead of the
+// S=QK^T MMA, which runs at most 2 chunks ahead of the softmax, so a slot is
+// never rewritten before the softmax has read it.
+constexpr int kMetaRing = 16;
 
-template <int D, int N>
+template <int D, int N, int CTAS>
 struct PrefillCfg {
   static constexpr int kRegions = D / 64;               // 64-column (128 B) slabs
   static constexpr int kQBytes = kTileM * D * 2;
   static constexpr int kKVBytes = N * D * 2;            // one K (or V) chunk
-  static constexpr int kSmemBudget = 227 * 1024 - 2048;
-  static constexpr int kStagesFit = (kSmemBudget - 1024 - kQBytes) / (2 * kKVBytes);
-  static constexpr int kStages = kStagesFit > 4 ? 4 : kStagesFit;
-  static constexpr int kSmemBytes = 1024 + kQBytes + kStages * 2 * kKVBytes;
-  static_assert(kStages >= 2, "not enough shared memory for a 2-stage pipeline");
+  // TMEM: O in columns [0, D), two S/P buffers of kSStride columns after it.
+  static constexpr int kSStride = N < 32 ? 32 : N;
+  static constexpr int kTmemNeed = D + 2 * kSStride;
+  static constexpr int kTmemCols = kTmemNeed <= 32 ? 32 : kTmemNeed <= 64 ? 64 : kTmemNeed <= 128 ? 128
+                                   : kTmemNeed <= 256 ? 256 : 512;
+  static_assert(kTmemCols * CTAS <= 512, "TMEM over-subscribed");
+  // 228 KB of shared memory per SM, of which 1 KB per resident CTA is reserved
+  // by the hardware and 1 KB holds this kernel's static shared data.
+  static constexpr int kSmemBudget = (233472 / CTAS) - 2048;
+  static constexpr int kBufs = (kSmemBudget - kQBytes) / kKVBytes;  // K + V chunk buffers
+  static constexpr int kKHalf = kBufs / 2 + (kBufs & 1);
+  static constexpr int kKStages = kKHalf > 4 ? 4 : kKHalf;
+  static constexpr int kVStages = (kBufs - kKStages) > 4 ? 4 : (kBufs - kKStages);
+  static constexpr int kSmemBytes = kQBytes + (kKStages + kVStages) * kKVBytes;
+  static_assert(kVStages >= 2, "not enough shared memory for the K/V rings");
+  static_assert(kKStages + 3 < kMetaRing, "meta ring too short");
 };
 
 // Chunk stream of one tile: sorted union of up to kMaxSeg CSR rows, each key
-// block expanded into `nsub` chunks of N keys.
+// block expanded into `nsub` chunks of N keys. Each segment keeps its current
+// and next index in registers and the load of the one after is issued a whole
+// chunk before it is needed (unconditional, at a clamped index: a select on a
+// load result would stall the producer on every chunk).
 struct ChunkStream {
   const int32_t* pairs;
   int ptr[kMaxSeg];
   int end[kMaxSeg];
+  int headv[kMaxSeg];
+  int nextv[kMaxSeg];
   int nseg;
   int nsub;
   int sub;
   int kb;
   uint32_t mask;
+
+  __device__ __forceinline__ static int clamp_idx(int i, int e) { return max(0, min(i, e - 1)); }
 
   __device__ void init(const PrefillParams& p, int h, int qb0, int nseg_, int nsub_) {
     pairs = p.pairs + (int64_t)h * p.pairs_stride;
@@ -87,6 +123,11 @@ struct ChunkStream {
         ptr[s] = end[s] = 0;
       }
     }
+#pragma unroll
+    for (int s = 0; s < kMaxSeg; ++s) {
+      headv[s] = __ldg(pairs + clamp_idx(ptr[s], end[s]));
+      nextv[s] = __ldg(pairs + clamp_idx(ptr[s] + 1, end[s]));
+    }
     sub = nsub;  // forces an advance on the first next()
     kb = -1;
     mask = 0;
@@ -100,14 +141,16 @@ struct ChunkStream {
     int best = 0x7fffffff;
 #pragma unroll
     for (int s = 0; s < kMaxSeg; ++s)
-      if (s < nseg && ptr[s] < end[s]) best = min(best, __ldg(pairs + ptr[s]));
+      if (s < nseg && ptr[s] < end[s]) best = min(best, headv[s]);
     if (best == 0x7fffffff) return false;
     uint32_t m = 0;
 #pragma unroll
     for (int s = 0; s < kMaxSeg; ++s)
-      if (s < nseg && ptr[s] < end[s] && __ldg(pairs + ptr[s]) == best) {
+      if (s < nseg && ptr[s] < end[s] && headv[s] == best) {
         m |= 1u << s;
         ++ptr[s];
+        headv[s] = nextv[s];
+        nextv[s] = __ldg(pairs + clamp_idx(ptr[s] + 1, end[s]));
       }
     kb = best;
     mask = m;
@@ -120,66 +163,68 @@ struct TileCoord {
   int b, h, q0, qb0, nseg, nsub;
 };
 
+// Head-major order (consecutive tiles share one (b, head), so its K/V stays in
+// L2), heaviest (last) query tile of each head first.
+template <int N>
 __device__ __forceinline__ TileCoord tile_coord(const PrefillParams& p, int t) {
-  const int bh_total = p.B * p.Hq;
-  const int qt = p.nqt - 1 - t / bh_total;  // heaviest (last) query tiles first
-  const int bh = t % bh_total;
+  const int bh = t / p.nqt;
+  const int qt = p.nqt - 1 - t % p.nqt;
   TileCoord c;
   c.b = bh / p.Hq;
   c.h = bh % p.Hq;
   c.q0 = qt * kTileM;
-  if (p.bs <= kTileM) {
-    c.qb0 = c.q0 / p.bs;
-    c.nseg = min(kTileM / p.bs, p.nqb - c.qb0);
-    c.nsub = 1;
-  } else {
-    c.qb0 = c.q0 / p.bs;
-    c.nseg = 1;
-    c.nsub = p.bs / kTileM;
-  }
+  c.qb0 = c.q0 / p.bs;
+  c.nseg = p.bs < kTileM ? min(kTileM / p.bs, p.nqb - c.qb0) : 1;
+  c.nsub = p.bs > N ? p.bs / N : 1;
   return c;
 }
 
-template <int D, int N>
-__global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_constant__ PrefillParams p) {
-  using Cfg = PrefillCfg<D, N>;
-  constexpr int NST = Cfg::kStages;
+template <int D, int N, int CTAS>
+__global__ void __launch_bounds__(kThreads, CTAS) prefill_kernel(const __grid_constant__ PrefillParams p) {
+  using Cfg = PrefillCfg<D, N, CTAS>;
+  constexpr uint32_t SB = D;                  // first S/P buffer column
+  constexpr uint32_t SS = Cfg::kSStride;      // S/P buffer stride (columns)
+  constexpr int NSK = Cfg::kKStages;
+  constexpr int NSV = Cfg::kVStages;
   constexpr int R = Cfg::kRegions;
 
   __shared__ __align__(8) uint64_t bar_q_full, bar_q_empty, bar_o_empty, bar_drain;
-  __shared__ __align__(8) uint64_t bar_k_full[NST], bar_v_full[NST], bar_kv_empty[NST];
-  __shared__ __align__(8) uint64_t bar_s_full[2], bar_p_full[2], bar_pv_done[2];
-  __shared__ int meta_key0[NST];
-  __shared__ uint32_t meta_mask[NST];
-  __shared__ int meta_last[NST];
+  __shared__ __align__(8) uint64_t bar_k_full[NSK], bar_k_empty[NSK], bar_v_full[NSV], bar_v_empty[NSV];
+  __shared__ __align__(8) uint64_t bar_p_full[2];
+  __shared__ __align__(8) uint64_t bar_meta[kMetaRing];
+  __shared__ int meta_key0[kMetaRing];
+  __shared__ uint32_t meta_mask[kMetaRing];
+  __shared__ int meta_last[kMetaRing];
   __shared__ uint32_t tmem_base_sh;
   __shared__ int abort_flag;
 
-  extern __shared__ uint8_t smem_raw[];
-  const uint32_t smem_base = (smem_u32(smem_raw) + 1023u) & ~1023u;
-  const uint32_t sQ = smem_base;
+  // Dynamic shared memory: Q | K ring | V ring, 1024-byte aligned for SWIZZLE_128B.
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  const uint32_t sQ = smem_u32(smem_raw);
   const uint32_t sK = sQ + Cfg::kQBytes;
-  const uint32_t sV = sK + NST * Cfg::kKVBytes;
+  const uint32_t sV = sK + NSK * Cfg::kKVBytes;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int ntiles = p.nqt * p.B * p.Hq;
+  const bool misaligned = (sQ & 1023u) != 0;
 
   if (threadIdx.x == 0) {
+    if (misaligned) record_error(p.err, SA_DEV_ERR_INDEX);
     mbar_init(smem_u32(&bar_q_full), 1);
     mbar_init(smem_u32(&bar_q_empty), 1);
     mbar_init(smem_u32(&bar_o_empty), 128);
     mbar_init(smem_u32(&bar_drain), 1);
-    for (int i = 0; i < NST; ++i) {
+    for (int i = 0; i < NSK; ++i) {
       mbar_init(smem_u32(&bar_k_full[i]), 1);
+      mbar_init(smem_u32(&bar_k_empty[i]), 1);
+    }
+    for (int i = 0; i < NSV; ++i) {
       mbar_init(smem_u32(&bar_v_full[i]), 1);
-      mbar_init(smem_u32(&bar_kv_empty[i]), 1);
+      mbar_init(smem_u32(&bar_v_empty[i]), 1);
     }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(smem_u32(&bar_s_full[i]), 1);
-      mbar_init(smem_u32(&bar_p_full[i]), 128);
-      mbar_init(smem_u32(&bar_pv_done[i]), 1);
-    }
+    for (int i = 0; i < kMetaRing; ++i) mbar_init(smem_u32(&bar_meta[i]), 1);
+    for (int i = 0; i < 2; ++i) mbar_init(smem_u32(&bar_p_full[i]), 128);
     abort_flag = 0;
     fence_mbar_init();
   }
@@ -189,7 +234,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
     tma_prefetch_desc(&p.tm_v);
   }
   if (warp == 1) {
-    tmem_alloc(smem_u32(&tmem_base_sh), 512);
+    tmem_alloc(smem_u32(&tmem_base_sh), Cfg::kTmemCols);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -198,15 +243,18 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
   const uint32_t tmem = tmem_base_sh;
   volatile int* abort_v = &abort_flag;
 
-  if (warp == 0) {
+  if (misaligned) {
+    // dynamic shared memory not 1024-byte aligned (recorded above): do nothing
+  } else if (warp == 0) {
     // ------------------------------------------------------------------ producer
+    // One thread. Per chunk: metadata (+ its barrier), K into the K ring once
+    // its slot's S=QK^T retired, V into the V ring once its slot's PV retired.
     if (lane == 0) {
-      uint32_t g = 0;  // chunks issued by this CTA
-      int it = 0;
-      int q_issued = 0;
+      uint32_t g = 0;
+      int it = 0, q_issued = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x, ++it) {
-        const TileCoord c = tile_coord(p, t);
+        const TileCoord c = tile_coord<N>(p, t);
         const int kvh = c.h / p.group;
         if (it > 0 && !(ok = mbar_wait(smem_u32(&bar_q_empty), (it - 1) & 1, abort_v, p.err))) break;
         mbar_arrive_expect_tx(smem_u32(&bar_q_full), Cfg::kQBytes);
@@ -214,7 +262,6 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
         for (int r = 0; r < R; ++r)
           tma_load_4d(sQ + r * kTileM * 128, &p.tm_q, smem_u32(&bar_q_full), r * 64, c.q0, c.h, c.b);
         ++q_issued;
-
         ChunkStream cs;
         cs.init(p, c.h, c.qb0, c.nseg, c.nsub);
         bool have = cs.next();
@@ -223,31 +270,36 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
         int cur_sub = have ? cs.sub : 0;
         while (true) {
           const bool more = have && cs.next();
-          const int st = g % NST;
-          if (g >= (uint32_t)NST &&
-              !(ok = mbar_wait(smem_u32(&bar_kv_empty[st]), ((g / NST) - 1) & 1, abort_v, p.err)))
-            break;
           int key0 = cur_kb * p.bs + cur_sub * N;
-          if (cur_kb < 0 || key0 < 0 || cur_kb >= (0x7fffffff / max(p.bs, 1)) ) {
-            // malformed index: load block 0, mask everything
-            record_error(p.err, SA_DEV_ERR_INDEX);
+          if (cur_kb < 0 || cur_kb >= (0x7fffffff / max(p.bs, 1))) {
+            record_error(p.err, SA_DEV_ERR_INDEX);  // malformed index: load block 0, mask all
             key0 = 0;
             cur_mask = 0;
           }
-          meta_key0[st] = key0;
-          meta_mask[st] = cur_mask;
-          meta_last[st] = more ? 0 : 1;
           const int kcoord = min(key0, p.T_k);  // fully out-of-range chunks read zeros
-          mbar_arrive_expect_tx(smem_u32(&bar_k_full[st]), Cfg::kKVBytes);
+          const int ks = g % NSK, vs = g % NSV, ms = g % kMetaRing;
+          if (g >= (uint32_t)NSK &&
+              !(ok = mbar_wait(smem_u32(&bar_k_empty[ks]), ((g / NSK) - 1) & 1, abort_v, p.err)))
+            break;
+          meta_key0[ms] = key0;
+          meta_mask[ms] = cur_mask;
+          meta_last[ms] = more ? 0 : 1;
+          mbar_arrive(smem_u32(&bar_meta[ms]));
+          mbar_arrive_expect_tx(smem_u32(&bar_k_full[ks]), Cfg::kKVBytes);
 #pragma unroll
           for (int r = 0; r < R; ++r)
-            tma_load_4d(sK + st * Cfg::kKVBytes + r * N * 128, &p.tm_k, smem_u32(&bar_k_full[st]),
-                        r * 64, kcoord, kvh, c.b);
-          mbar_arrive_expect_tx(smem_u32(&bar_v_full[st]), Cfg::kKVBytes);
+            tma_load_4d(sK + ks * Cfg::kKVBytes + r * N * 128, &p.tm_k, smem_u32(&bar_k_full[ks]), r * 64, kcoord,
+                        kvh, c.b);
+          SA_TRACE(g, 13);
+          if (g >= (uint32_t)NSV &&
+              !(ok = mbar_wait(smem_u32(&bar_v_empty[vs]), ((g / NSV) - 1) & 1, abort_v, p.err)))
+            break;
+          mbar_arrive_expect_tx(smem_u32(&bar_v_full[vs]), Cfg::kKVBytes);
 #pragma unroll
           for (int r = 0; r < R; ++r)
-            tma_load_4d(sV + st * Cfg::kKVBytes + r * N * 128, &p.tm_v, smem_u32(&bar_v_full[st]),
-                        r * 64, kcoord, kvh, c.b);
+            tma_load_4d(sV + vs * Cfg::kKVBytes + r * N * 128, &p.tm_v, smem_u32(&bar_v_full[vs]), r * 64, kcoord,
+                        kvh, c.b);
+          SA_TRACE(g, 14);
           ++g;
           if (!more) break;
           cur_kb = cs.kb;
@@ -258,12 +310,13 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
       // Drain: wait (bounded, ignoring the abort flag) for copies still in flight.
       int zero = 0;
       volatile int* never = &zero;
-      const uint32_t n_recent = g < (uint32_t)NST ? g : (uint32_t)NST;
-      for (uint32_t i = 0; i < n_recent; ++i) {
+      for (uint32_t i = 0; i < (g < (uint32_t)NSK ? g : (uint32_t)NSK); ++i) {
         const uint32_t gi = g - 1 - i;
-        const int st = gi % NST;
-        mbar_wait(smem_u32(&bar_k_full[st]), (gi / NST) & 1, never, nullptr);
-        mbar_wait(smem_u32(&bar_v_full[st]), (gi / NST) & 1, never, nullptr);
+        mbar_wait(smem_u32(&bar_k_full[gi % NSK]), (gi / NSK) & 1, never, nullptr);
+      }
+      for (uint32_t i = 0; i < (g < (uint32_t)NSV ? g : (uint32_t)NSV); ++i) {
+        const uint32_t gi = g - 1 - i;
+        mbar_wait(smem_u32(&bar_v_full[gi % NSV]), (gi / NSV) & 1, never, nullptr);
       }
       if (q_issued > 0) mbar_wait(smem_u32(&bar_q_full), (q_issued - 1) & 1, never, nullptr);
     }
@@ -272,60 +325,62 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
     if (lane == 0) {
       constexpr uint32_t idesc_s = idesc_bf16_f32(128, N, false);
       constexpr uint32_t idesc_pv = idesc_bf16_f32(128, D, true);
+      // Descriptors are built once; an operand's start address is a constant
+      // offset (16-byte units) added to the base descriptor.
+      const uint64_t q_desc = smem_desc_sw128(sQ, 16, 1024);
+      const uint64_t k_desc = smem_desc_sw128(sK, 16, 1024);
+      const uint64_t v_desc = smem_desc_sw128(sV, N * 128, 1024);
       uint32_t g = 0;
       int it = 0;
       bool ok = true;
+      // S = Q K^T for chunk gg. Its commit on the K slot both frees the slot
+      // and tells the softmax that S is in TMEM.
       auto issue_s = [&](uint32_t gg) {
-        const int st = gg % NST;
-        const uint32_t d = tmem + 128 + (gg & 1) * 128;
+        const int ks = gg % NSK;
+        const uint32_t d = tmem + SB + (gg & 1) * SS;
+        const uint64_t kst = k_desc + (uint64_t)((ks * Cfg::kKVBytes) >> 4);
 #pragma unroll
         for (int k = 0; k < D / 16; ++k) {
           const int r = k >> 2, kk = k & 3;
-          const uint64_t a = smem_desc_sw128(sQ + r * kTileM * 128 + kk * 32, 16, 1024);
-          const uint64_t b = smem_desc_sw128(sK + st * Cfg::kKVBytes + r * N * 128 + kk * 32, 16, 1024);
-          mma_ss(d, a, b, idesc_s, k > 0 ? 1u : 0u);
+          mma_ss(d, q_desc + ((r * kTileM * 128 + kk * 32) >> 4), kst + ((r * N * 128 + kk * 32) >> 4), idesc_s,
+                 k > 0 ? 1u : 0u);
         }
+        mma_commit(smem_u32(&bar_k_empty[ks]));
+        SA_TRACE(gg, 5);
       };
       for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x, ++it) {
         if (!(ok = mbar_wait(smem_u32(&bar_q_full), it & 1, abort_v, p.err))) break;
         tc_fence_after();
-        int st = g % NST;
-        if (!(ok = mbar_wait(smem_u32(&bar_k_full[st]), (g / NST) & 1, abort_v, p.err))) break;
+        if (!(ok = mbar_wait(smem_u32(&bar_k_full[g % NSK]), (g / NSK) & 1, abort_v, p.err))) break;
         tc_fence_after();
-        int last = meta_last[st];
+        int last = meta_last[g % kMetaRing];
         issue_s(g);
-        mma_commit(smem_u32(&bar_s_full[g & 1]));
         if (last) mma_commit(smem_u32(&bar_q_empty));
-        bool first = true;
+        const uint32_t g0 = g;
         while (true) {
           const bool cur_last = last;
           const uint32_t gn = g + 1;
           if (!cur_last) {
-            const int stn = gn % NST;
-            if (!(ok = mbar_wait(smem_u32(&bar_k_full[stn]), (gn / NST) & 1, abort_v, p.err))) break;
+            if (!(ok = mbar_wait(smem_u32(&bar_k_full[gn % NSK]), (gn / NSK) & 1, abort_v, p.err))) break;
             tc_fence_after();
-            last = meta_last[stn];
+            last = meta_last[gn % kMetaRing];
             issue_s(gn);
-            mma_commit(smem_u32(&bar_s_full[gn & 1]));
             if (last) mma_commit(smem_u32(&bar_q_empty));
           }
           if (!(ok = mbar_wait(smem_u32(&bar_p_full[g & 1]), (g >> 1) & 1, abort_v, p.err))) break;
-          if (first && it > 0 &&
-              !(ok = mbar_wait(smem_u32(&bar_o_empty), (it - 1) & 1, abort_v, p.err)))
-            break;
-          if (!(ok = mbar_wait(smem_u32(&bar_v_full[st]), (g / NST) & 1, abort_v, p.err))) break;
+          SA_TRACE(g, 6);
+          if (g == g0 && it > 0 && !(ok = mbar_wait(smem_u32(&bar_o_empty), (it - 1) & 1, abort_v, p.err))) break;
+          const int vs = g % NSV;
+          if (!(ok = mbar_wait(smem_u32(&bar_v_full[vs]), (g / NSV) & 1, abort_v, p.err))) break;
           tc_fence_after();
-          const uint32_t pbuf = tmem + 128 + (g & 1) * 128;
+          const uint32_t pbuf = tmem + SB + (g & 1) * SS;
+          const uint64_t vst = v_desc + (uint64_t)((vs * Cfg::kKVBytes) >> 4);
+          const uint32_t acc0 = g != g0 ? 1u : 0u;
 #pragma unroll
-          for (int k = 0; k < N / 16; ++k) {
-            const uint64_t b = smem_desc_sw128(sV + st * Cfg::kKVBytes + k * 2048, N * 128, 1024);
-            mma_ts(tmem, pbuf + k * 8, b, idesc_pv, (!first || k > 0) ? 1u : 0u);
-          }
-          mma_commit(smem_u32(&bar_kv_empty[st]));
-          mma_commit(smem_u32(&bar_pv_done[g & 1]));
+          for (int k = 0; k < N / 16; ++k) mma_ts(tmem, pbuf + k * 8, vst + ((k * 2048) >> 4), idesc_pv, k > 0 ? 1u : acc0);
+          mma_commit(smem_u32(&bar_v_empty[vs]));  // PV_g retired: V slot free, O holds chunk g
+          SA_TRACE(g, 7);
           g = gn;
-          st = g % NST;
-          first = false;
           if (cur_last) break;
         }
       }
@@ -336,6 +391,9 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
     }
   } else {
     // ------------------------------------------------------------------ softmax
+    // "S_j in TMEM" is completion of K slot j%NSK and "PV_j retired" that of V
+    // slot j%NSV: neither can advance a second phase before this warpgroup has
+    // consumed chunk j, so the parity waits are exact.
     const int wr = warp & 3;  // TMEM lane quadrant this warp may access
     const int row = wr * 32 + lane;
     const uint32_t lane_base = (uint32_t)(wr * 32) << 16;
@@ -344,7 +402,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
     int it = 0;
     bool ok = true;
     for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x, ++it) {
-      const TileCoord c = tile_coord(p, t);
+      const TileCoord c = tile_coord<N>(p, t);
       const int q_local = c.q0 + row;
       const int q_abs = q_local + (p.T_k - p.T_q);
       const bool row_ok = q_local < p.T_q;
@@ -353,59 +411,63 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
       float l = 0.f;
       bool first = true;
       while (true) {
-        const int st = g % NST;
-        ok = mbar_wait(smem_u32(&bar_k_full[st]), (g / NST) & 1, abort_v, p.err);
+        const int ms = g % kMetaRing;
+        ok = mbar_wait(smem_u32(&bar_meta[ms]), (g / kMetaRing) & 1, abort_v, p.err);
         if (!__all_sync(FULL, ok)) { ok = false; break; }
-        const int key0 = meta_key0[st];
-        const uint32_t mask = meta_mask[st];
-        const int last = meta_last[st];
-        ok = mbar_wait(smem_u32(&bar_s_full[g & 1]), (g >> 1) & 1, abort_v, p.err);
+        const int key0 = meta_key0[ms];
+        const uint32_t mask = meta_mask[ms];
+        const int last = meta_last[ms];
+        if (threadIdx.x == 64) SA_TRACE(g, 0);
+        ok = mbar_wait(smem_u32(&bar_k_empty[g % NSK]), (g / NSK) & 1, abort_v, p.err);
+        if (threadIdx.x == 64) SA_TRACE(g, 1);
         if (!__all_sync(FULL, ok)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t sbuf = tmem + lane_base + 128 + (g & 1) * 128;
+        const uint32_t sbuf = tmem + lane_base + SB + (g & 1) * SS;
         float s[N];
         if constexpr (N >= 32) {
+          uint32_t r32[N / 32][32];
+#pragma unroll
+          for (int cc = 0; cc < N / 32; ++cc) tmem_ld32(sbuf + cc * 32, r32[cc]);
+          tmem_wait_ld();
 #pragma unroll
           for (int cc = 0; cc < N / 32; ++cc) {
-            uint32_t r32[32];
-            tmem_ld32(sbuf + cc * 32, r32);
-            tmem_wait_ld();
+            reg_fence32(r32[cc]);
 #pragma unroll
-            for (int i = 0; i < 32; ++i) s[cc * 32 + i] = __uint_as_float(r32[i]);
+            for (int i = 0; i < 32; ++i) s[cc * 32 + i] = __uint_as_float(r32[cc][i]);
           }
         } else {
           uint32_t r16[16];
           tmem_ld16(sbuf, r16);
           tmem_wait_ld();
+          reg_fence16(r16);
 #pragma unroll
           for (int i = 0; i < 16; ++i) s[i] = __uint_as_float(r16[i]);
         }
+        if (threadIdx.x == 64) SA_TRACE(g, 2);
         const bool mine = row_ok && ((mask >> seg) & 1u);
         const bool full_ok = mine && (key0 + N - 1 <= q_abs) && (key0 + N <= p.T_k);
-        float mblk = -INFINITY;
-        if (full_ok) {
-#pragma unroll
-          for (int i = 0; i < N; ++i) {
-            s[i] *= p.scale_log2;
-            mblk = fmaxf(mblk, s[i]);
-          }
-        } else {
+        if (!full_ok) {
           const int lim = min(q_abs, p.T_k - 1) - key0;  // valid columns: i <= lim
 #pragma unroll
-          for (int i = 0; i < N; ++i) {
-            const bool v = mine && (i <= lim);
-            s[i] = v ? s[i] * p.scale_log2 : -INFINITY;
-            mblk = fmaxf(mblk, s[i]);
-          }
+          for (int i = 0; i < N; ++i) s[i] = (mine && i <= lim) ? s[i] : -INFINITY;
         }
-        const float m_new = fmaxf(m_ref, mblk);
+        // Raw-score row max with 8 independent chains; the positive scale is
+        // folded into the exponent below.
+        float mx8[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) mx8[i] = s[i];
+#pragma unroll
+        for (int i = 8; i < N; ++i) mx8[i & 7] = fmaxf(mx8[i & 7], s[i]);
+        const float mraw = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                                 fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+        const float m_new = fmaxf(m_ref, mraw * p.scale_log2);
         if (first) {
           m_ref = m_new;
         } else {
           const bool need = m_new > m_ref + 8.0f;
           if (__any_sync(FULL, need)) {
             // O still holds the previous chunk's PV: wait for it, then rescale.
-            ok = mbar_wait(smem_u32(&bar_pv_done[(g - 1) & 1]), ((g - 1) >> 1) & 1, abort_v, p.err);
+            ok = mbar_wait(smem_u32(&bar_v_empty[(g - 1) % NSV]), ((g - 1) / NSV) & 1, abort_v, p.err);
             if (!__all_sync(FULL, ok)) { ok = false; break; }
             tc_fence_after();
             const float alpha = need ? ex2(m_ref - m_new) : 1.0f;
@@ -414,6 +476,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
               uint32_t o32[32];
               tmem_ld32(tmem + lane_base + cc * 32, o32);
               tmem_wait_ld();
+              reg_fence32(o32);
 #pragma unroll
               for (int i = 0; i < 32; ++i) o32[i] = __float_as_uint(__uint_as_float(o32[i]) * alpha);
               tmem_st32(tmem + lane_base + cc * 32, o32);
@@ -426,16 +489,21 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
           }
         }
         const float m_use = (m_ref == -INFINITY) ? 0.f : m_ref;
+        const float nm = -m_use;
         uint32_t pk[N / 2];
-        float rs = 0.f;
+        float rs8[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) rs8[i] = 0.f;
 #pragma unroll
         for (int i = 0; i < N / 2; ++i) {
-          const float p0 = ex2(s[2 * i] - m_use);
-          const float p1 = ex2(s[2 * i + 1] - m_use);
-          rs += p0 + p1;
+          const float p0 = ex2(fmaf(s[2 * i], p.scale_log2, nm));
+          const float p1 = ex2(fmaf(s[2 * i + 1], p.scale_log2, nm));
+          rs8[(2 * i) & 7] += p0;
+          rs8[(2 * i + 1) & 7] += p1;
           pk[i] = pack_bf16(p0, p1);
         }
-        l += rs;
+        l += ((rs8[0] + rs8[1]) + (rs8[2] + rs8[3])) + ((rs8[4] + rs8[5]) + (rs8[6] + rs8[7]));
+        if (threadIdx.x == 64) SA_TRACE(g, 3);
         // P (bf16 pairs) overwrites the first N/2 columns of this S buffer.
         if constexpr (N / 2 >= 32) {
 #pragma unroll
@@ -459,41 +527,44 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
         tmem_wait_st();
         tc_fence_before();
         mbar_arrive(smem_u32(&bar_p_full[g & 1]));
+        if (threadIdx.x == 64) SA_TRACE(g, 4);
         ++g;
         first = false;
         if (last) break;
       }
       if (!ok) break;
       // ---------------------------------------------------------------- epilogue
-      ok = mbar_wait(smem_u32(&bar_pv_done[(g - 1) & 1]), ((g - 1) >> 1) & 1, abort_v, p.err);
+      ok = mbar_wait(smem_u32(&bar_v_empty[(g - 1) % NSV]), ((g - 1) / NSV) & 1, abort_v, p.err);
       if (!__all_sync(FULL, ok)) { ok = false; break; }
       tc_fence_after();
       const float inv = l > 0.f ? 1.0f / l : 0.f;
       __nv_bfloat16* orow = p.out + (int64_t)c.b * p.o_sb + (int64_t)c.h * p.o_sh + (int64_t)q_local * p.o_st;
+      uint32_t o32[D / 32][32];
+#pragma unroll
+      for (int cc = 0; cc < D / 32; ++cc) tmem_ld32(tmem + lane_base + cc * 32, o32[cc]);
+      tmem_wait_ld();
+      tc_fence_before();
+      mbar_arrive(smem_u32(&bar_o_empty));  // O is in registers: the next tile may overwrite TMEM
 #pragma unroll
       for (int cc = 0; cc < D / 32; ++cc) {
-        uint32_t o32[32];
-        tmem_ld32(tmem + lane_base + cc * 32, o32);
-        tmem_wait_ld();
+        reg_fence32(o32[cc]);
         if (row_ok) {
           uint32_t w[16];
 #pragma unroll
           for (int i = 0; i < 16; ++i)
-            w[i] = pack_bf16(__uint_as_float(o32[2 * i]) * inv, __uint_as_float(o32[2 * i + 1]) * inv);
+            w[i] = pack_bf16(__uint_as_float(o32[cc][2 * i]) * inv, __uint_as_float(o32[cc][2 * i + 1]) * inv);
           uint4* dst = reinterpret_cast<uint4*>(orow + cc * 32);
 #pragma unroll
           for (int i = 0; i < 4; ++i) dst[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
         }
       }
-      tc_fence_before();
-      mbar_arrive(smem_u32(&bar_o_empty));
     }
   }
 
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 1) tmem_dealloc(tmem, 512);
+  if (warp == 1) tmem_dealloc(tmem, Cfg::kTmemCols);
 }
 
 // ---------------------------------------------------------------------------
@@ -534,16 +605,16 @@ static int make_map(CUtensorMap* m, const void* base, int B, int H, int T, int D
   return SA_OK;
 }
 
-template <int D, int N>
-static int launch_prefill(const PrefillParams& prm, int grid, cudaStream_t stream) {
-  using Cfg = PrefillCfg<D, N>;
-  static bool attr_set = false;  // per process; the attribute is per function and device-independent
-  if (!attr_set) {
-    SA_CHECK_CUDA(cudaFuncSetAttribute(prefill_kernel<D, N>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       Cfg::kSmemBytes));
-    attr_set = true;
-  }
-  prefill_kernel<D, N><<<grid, kThreads, Cfg::kSmemBytes, stream>>>(prm);
+template <int D, int N, int CTAS>
+static int launch_prefill(const PrefillParams& prm, int64_t ntiles, int sms, cudaStream_t stream) {
+  using Cfg = PrefillCfg<D, N, CTAS>;
+  SA_CHECK_CUDA(cudaFuncSetAttribute(prefill_kernel<D, N, CTAS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     Cfg::kSmemBytes));
+  SA_CHECK_CUDA(cudaFuncSetAttribute(prefill_kernel<D, N, CTAS>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                     100));
+  const int64_t slots = (int64_t)sms * CTAS;
+  const int grid = (int)(ntiles < slots ? ntiles : slots);
+  prefill_kernel<D, N, CTAS><<<grid, kThreads, Cfg::kSmemBytes, stream>>>(prm);
   SA_CHECK_CUDA(cudaGetLastError());
   return SA_OK;
 }
@@ -551,6 +622,15 @@ static int launch_prefill(const PrefillParams& prm, int grid, cudaStream_t strea
 }  // namespace sa
 
 using namespace sa;
+
+static int sa_prefill_chunk() {
+  static int v = 0;
+  if (!v) {
+    const char* e = getenv("SA_PREFILL_CHUNK");
+    v = (e && atoi(e) == 128) ? 128 : 64;
+  }
+  return v;
+}
 
 static bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }
 
@@ -584,7 +664,8 @@ extern "C" int sa_prefill_fwd(const sa_attn_args* a, sa_stream_t stream_) {
   if (rc) return rc;
   cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
   const int bs = a->block_size;
-  const int N = bs >= 128 ? 128 : bs;
+  const int chunk = sa_prefill_chunk();
+  const int N = bs >= chunk ? chunk : bs;
   PrefillParams prm;
   memset(&prm, 0, sizeof(prm));
   if ((rc = make_map(&prm.tm_q, a->q, a->B, a->Hq, a->T_q, a->D, a->q_strides, kTileM, "q"))) return rc;
@@ -612,16 +693,31 @@ extern "C" int sa_prefill_fwd(const sa_attn_args* a, sa_stream_t stream_) {
   if (ntiles > 0x7fffffff) return sa_fail(SA_ERR_INVALID, "too many tiles");
   int sms = a->num_sms > 0 ? a->num_sms : sa_num_sms();
   if (sms <= 0) return sa_fail(SA_ERR_CUDA, "cannot query SM count");
-  const int grid = (int)(ntiles < sms ? ntiles : sms);
-  switch (a->D * 1000 + N) {
-    case 128128: return launch_prefill<128, 128>(prm, grid, stream);
-    case 128064: return launch_prefill<128, 64>(prm, grid, stream);
-    case 128032: return launch_prefill<128, 32>(prm, grid, stream);
-    case 128016: return launch_prefill<128, 16>(prm, grid, stream);
-    case 64128: return launch_prefill<64, 128>(prm, grid, stream);
-    case 64064: return launch_prefill<64, 64>(prm, grid, stream);
-    case 64032: return launch_prefill<64, 32>(prm, grid, stream);
-    case 64016: return launch_prefill<64, 16>(prm, grid, stream);
+  // Chunk size: 64 keys with two CTAs per SM (default; their softmax
+  // warpgroups interleave on the tensor core), or 128 keys with one CTA per SM
+  // (SA_PREFILL_CHUNK=128).
+  switch (a->D * 10000 + N) {
+    case 1280128: return launch_prefill<128, 128, 1>(prm, ntiles, sms, stream);
+    case 1280064: return launch_prefill<128, 64, 2>(prm, ntiles, sms, stream);
+    case 1280032: return launch_prefill<128, 32, 2>(prm, ntiles, sms, stream);
+    case 1280016: return launch_prefill<128, 16, 2>(prm, ntiles, sms, stream);
+    case 640128: return launch_prefill<64, 128, 1>(prm, ntiles, sms, stream);
+    case 640064: return launch_prefill<64, 64, 2>(prm, ntiles, sms, stream);
+    case 640032: return launch_prefill<64, 32, 2>(prm, ntiles, sms, stream);
+    case 640016: return launch_prefill<64, 16, 2>(prm, ntiles, sms, stream);
   }
   return sa_fail(SA_ERR_UNSUPPORTED, "no kernel for D=%d chunk=%d", a->D, N);
 }
+
+#ifdef SA_PHASE_TRACE
+extern "C" SA_API int sa_debug_trace_clear() {
+  static unsigned long long zeros[16 * 512];
+  SA_CHECK_CUDA(cudaMemcpyToSymbol(sa::g_sa_trace, zeros, sizeof(zeros)));
+  return SA_OK;
+}
+extern "C" SA_API int sa_debug_trace_read(unsigned long long* host, int n) {
+  SA_CHECK_CUDA(cudaDeviceSynchronize());
+  SA_CHECK_CUDA(cudaMemcpyFromSymbol(host, sa::g_sa_trace, sizeof(unsigned long long) * (n < 8192 ? n : 8192)));
+  return SA_OK;
+}
+#endif
