@@ -170,6 +170,24 @@ SA_API int sa_prefill_fwd(const sa_attn_args* args, sa_stream_t stream);
 SA_API int sa_decode_fwd(const sa_attn_args* args, int32_t n_split, float* partial_o,
                   float* partial_ml, sa_stream_t stream);
 
+/* ---------------------------------------------------------------------------
+ * sa_decode_fwd without caller scratch. No counterpart in the reference: it is
+ * for callers that cannot allocate device memory at call time (code that owns
+ * no allocator, such as a plugin running inside another framework's memory
+ * pool, or a serving loop that must not allocate while it runs). The split
+ * partials live in a fixed array compiled into this library, SA_DECODE_SCRATCH_FLOATS
+ * floats (16 MiB) that every GPU which loads the library keeps until exit;
+ * calls needing B*Hq*n_split*(D+2) floats beyond that fail with SA_ERR_INVALID.
+ * Nothing here calls cudaMalloc/cudaFree. The first call on a device looks up
+ * the array's device address (cudaGetSymbolAddress); make that first call
+ * before any stream capture. All calls share the one array: calls that overlap
+ * on the GPU (other streams, other threads) race and must be serialised by the
+ * caller. Every split result is fully rewritten by each call, so nothing has to
+ * start at zero. Same arguments, output and limits as sa_decode_fwd otherwise.
+ * ------------------------------------------------------------------------- */
+#define SA_DECODE_SCRATCH_FLOATS (4 * 1024 * 1024)
+SA_API int sa_decode_fwd_noalloc(const sa_attn_args* args, int32_t n_split, sa_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -26,6 +26,7 @@ EXPORTED = (
     "sa_kvlist_pairs",
     "sa_prefill_fwd",
     "sa_decode_fwd",
+    "sa_decode_fwd_noalloc",
 )
 
 SA_OK = 0
@@ -93,6 +94,7 @@ def load(path: str | os.PathLike | None = None) -> ctypes.CDLL:
     lib.sa_kvlist_pairs.argtypes = [_c_p, _c_i32, _c_i32, _c_i32, _c_p, _c_p, _c_i32, _c_p]
     lib.sa_prefill_fwd.argtypes = [ctypes.POINTER(AttnArgs), _c_p]
     lib.sa_decode_fwd.argtypes = [ctypes.POINTER(AttnArgs), _c_i32, _c_p, _c_p, _c_p]
+    lib.sa_decode_fwd_noalloc.argtypes = [ctypes.POINTER(AttnArgs), _c_i32, _c_p]
     for name in EXPORTED:
         if name not in ("sa_version", "sa_last_error"):
             getattr(lib, name).restype = ctypes.c_int

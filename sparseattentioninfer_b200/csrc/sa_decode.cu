@@ -447,3 +447,46 @@ extern "C" int sa_decode_fwd(const sa_attn_args* a, int32_t n_split, float* part
   if (rc) return rc;
   return sa_decode_launch(prm, a, reinterpret_cast<cudaStream_t>(stream));
 }
+
+// ---------------------------------------------------------------------------
+// Allocation-free decode: split partials in a library-owned device array.
+// ---------------------------------------------------------------------------
+static __device__ __align__(256) float g_sa_decode_scratch[SA_DECODE_SCRATCH_FLOATS];
+
+// Device address of g_sa_decode_scratch on the current device, looked up once
+// per device (the host-side symbol is not a device address).
+static int decode_scratch_ptr(float** out) {
+  static float* ptrs[64] = {nullptr};
+  int dev = 0;
+  SA_CHECK_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return sa_fail(SA_ERR_UNSUPPORTED, "device index %d out of range", dev);
+  if (!ptrs[dev]) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_sa_decode_scratch);
+    if (e != cudaSuccess) return sa_cuda_check(e, "cudaGetSymbolAddress(g_sa_decode_scratch)");
+    ptrs[dev] = static_cast<float*>(p);
+  }
+  *out = ptrs[dev];
+  return SA_OK;
+}
+
+extern "C" int sa_decode_fwd_noalloc(const sa_attn_args* a, int32_t n_split, sa_stream_t stream) {
+  if (!a) return sa_fail(SA_ERR_INVALID, "args is NULL");
+  if (n_split < 1 || n_split > 64) return sa_fail(SA_ERR_INVALID, "n_split %d not in [1, 64]", n_split);
+  if (a->B <= 0 || a->Hq <= 0 || (a->D != 64 && a->D != 128))
+    return sa_fail(SA_ERR_INVALID, "bad B/Hq/D (B=%d Hq=%d D=%d)", a->B, a->Hq, a->D);
+  const int64_t rows = (int64_t)a->B * a->Hq * n_split;
+  const int64_t need = rows * (a->D + 2);
+  if (need > (int64_t)SA_DECODE_SCRATCH_FLOATS)
+    return sa_fail(SA_ERR_INVALID,
+                   "decode scratch needs %lld floats (B*Hq*n_split*(D+2)), the built-in array holds %d; "
+                   "lower n_split or use sa_decode_fwd with caller scratch",
+                   (long long)need, (int)SA_DECODE_SCRATCH_FLOATS);
+  float* base = nullptr;
+  int rc = decode_scratch_ptr(&base);
+  if (rc) return rc;
+  DecodeParams prm;
+  rc = sa_decode_prepare(a, n_split, base, base + rows * a->D, &prm);
+  if (rc) return rc;
+  return sa_decode_launch(prm, a, reinterpret_cast<cudaStream_t>(stream));
+}
