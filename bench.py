@@ -333,7 +333,7 @@ def run_ours(args) -> None:
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                      "frac": achieved / peak, "peak_kind": f"{peak_kind} bf16 dense (burst)",
                      "traffic": traffic_from_profile("prefill_cfg2_ncu.txt"),
-                     "kernel": "sa::prefill_kernel<128,128>", "launch_ms": t_launch * 1e3},
+                     "kernel": "sa::prefill_kernel<128,64,2>", "traffic_note": "ncu dram read+write of one launch, profiles/prefill_cfg2_ncu.txt", "launch_ms": t_launch * 1e3},
         "e2e": {"value": total_flops * e2e_steps / e2e_elapsed / 1e12, "unit": "TFLOP/s",
                 "h2d_bytes_per_step": in_bytes, "d2h_bytes_per_step": q.numel() * 2,
                 "ms_per_step": e2e_elapsed / e2e_steps * 1e3,
@@ -346,6 +346,7 @@ def run_ours(args) -> None:
         hb = float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))
         line["decode"]["roofline_frac"] = line["decode"]["achieved_gbs"] / hb
         line["decode"]["peak_gbs"] = hb
+        line["decode"]["traffic"] = traffic_from_profile("decode_qwen3_4b_layer_ncu.txt")
     except Exception as e:  # noqa: BLE001
         line["decode"] = {"error": repr(e)}
     if world == 1 and not args.no_cpu_baseline:
