@@ -62,8 +62,13 @@ class CudaSm100Backend(AttentionBackend):
         key = (H, T_q, T_k, str(device))
         if key not in self._dense_cache:
             nkb = math.ceil(T_k / bs)
-            pairs, offsets = _ops.compile_bigbird([(bs, 0, nkb, 0)], H, T_q, T_k, bs, device=device)
+            nqb = math.ceil(T_q / bs)
+            qoff = (T_k - T_q) // bs
+            width = sum(min(qoff + q + 1, nkb) for q in range(nqb))  # exact nnz: no device read
+            pairs, offsets = _ops.compile_bigbird([(bs, 0, nkb, 0)], H, T_q, T_k, bs, device=device, width=width)
             self._dense_cache[key] = (pairs, offsets, bs)
+            while len(self._dense_cache) > 16:  # one entry per decode length: keep the recent ones
+                self._dense_cache.pop(next(iter(self._dense_cache)))
         return self._dense_cache[key]
 
     def forward(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, pattern: PatternMetadata) -> torch.Tensor:

@@ -172,6 +172,8 @@ class _BigBirdBase(SparsePattern):
             else:
                 keep = float("nan")  # computed lazily by keep_ratio_of() to stay sync-free
             self._csr_cache[key] = (pairs, offsets, keep)
+            while len(self._csr_cache) > 16:  # decode builds one entry per T_k: keep the recent ones
+                self._csr_cache.pop(next(iter(self._csr_cache)))
         pairs, offsets, keep = self._csr_cache[key]
         mask = None
         if self.materialize_mask:

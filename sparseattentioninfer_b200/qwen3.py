@@ -1,0 +1,285 @@
+"""Qwen3 attention hook: HF ``Qwen3Attention`` with the attention core on the B200 kernels.
+
+Mirrors sparse_llm/qwen3/integrations/modeling_sparse_qwen3.py
+(``Qwen3SparseKernelAttention`` :93-315, ``replace_qwen3_attention_with_sparse``
+:347-406, ``Qwen3SparseKernelForCausalLM`` :470-484) and the layer-block
+selection of sparse_llm/qwen3/experiment/layer_block_sparsity.py:193-223, with
+these deliberate differences:
+
+* ``forward`` takes transformers-5.x ``past_key_values`` (the reference's
+  ``past_key_value`` argument never receives the cache under transformers 5.x,
+  so its decode ran without one);
+* K/V keep their Hkv heads (no ``repeat_kv`` copy): the kernels read KV head
+  h // (Hq/Hkv);
+* a layer without a sparsity entry is truly dense (full causal attention via a
+  dense block CSR), whereas the reference's "0.0 sparsity" is still BigBird;
+* explicit per-group BigBird layouts per layer (``sparse_attention_layer_layouts``)
+  are accepted, the supported form of the reference's ``_layout_cache``
+  injection;
+* no fallback: the attention runs on the CUDA backend or raises.
+
+``PreallocatedKVCache`` is a transformers ``Cache`` whose layers hold a
+fixed-capacity [B, Hkv, T_max, D] buffer and return [:, :, :T] views, replacing
+the ``torch.cat`` growth of DynamicCache (one O(T) copy per step per layer).
+"""
+from __future__ import annotations
+
+from collections import OrderedDict
+from typing import Any, Optional, Sequence
+
+import torch
+from torch import nn
+from transformers.cache_utils import Cache, DynamicLayer
+from transformers.models.qwen3.configuration_qwen3 import Qwen3Config
+from transformers.models.qwen3.modeling_qwen3 import Qwen3Attention, Qwen3ForCausalLM, apply_rotary_pos_emb
+
+from .backend import CudaSm100Backend
+from .patterns import (
+    BigBirdKeepRatioPattern,
+    BigBirdPattern,
+    DenseCausalPattern,
+    LocalWindowPattern,
+    SparsePattern,
+)
+
+
+def _get(config, name: str, default):
+    return getattr(config, name, default)
+
+
+def normalize_group_sparsities(values, *, name: str = "group_sparsities"):
+    """sparse_config.py:20-27."""
+    if values is None:
+        return None
+    out = tuple(float(v) for v in values)
+    if any(not 0.0 <= v < 1.0 for v in out):
+        raise ValueError(f"{name} values must satisfy 0 <= sparsity < 1.")
+    return out
+
+
+def normalize_layer_group_sparsities(values, *, name: str = "layer_group_sparsities"):
+    """sparse_config.py:30-48."""
+    if values is None:
+        return None
+    return tuple(None if v is None else normalize_group_sparsities(v, name=f"{name}[{i}]")
+                 for i, v in enumerate(values))
+
+
+def build_layer_block_experiments(*, num_layers: int, num_groups: int, layer_span: int,
+                                  target_sparsity: float) -> list[dict[str, Any]]:
+    """layer_block_sparsity.py:193-223: contiguous blocks of ``layer_span`` layers get
+    ``target_sparsity`` in every KV group, the other layers 0.0."""
+    exps = []
+    for idx, start in enumerate(range(0, num_layers, layer_span)):
+        stop = min(start + layer_span, num_layers)
+        lgs = [[target_sparsity if start <= li < stop else 0.0] * num_groups for li in range(num_layers)]
+        mean = sum(v for row in lgs for v in row) / max(1, num_layers * num_groups)
+        slug = f"{target_sparsity:g}".replace(".", "p")
+        exps.append({"experiment_idx": idx, "label": f"exp_{idx:02d}_layers_{start}_{stop - 1}_s{slug}",
+                     "layer_start": start, "layer_end": stop - 1, "layer_count": stop - start,
+                     "target_sparsity": target_sparsity, "mean_sparsity": mean,
+                     "layer_group_sparsities": lgs})
+    return exps
+
+
+class _LRU(OrderedDict):
+    def __init__(self, cap: int):
+        super().__init__()
+        self.cap = cap
+
+    def put(self, k, v):
+        self[k] = v
+        self.move_to_end(k)
+        while len(self) > self.cap:
+            self.popitem(last=False)
+
+
+class Qwen3SparseKernelAttention(Qwen3Attention):
+    """HF Qwen3 attention with the attention core replaced by the cuda_sm100 backend."""
+
+    def __init__(self, config: Qwen3Config, layer_idx: int, *, backend_name: Optional[str] = None,
+                 window_size: Optional[int] = None, block_size: Optional[int] = None, group_sparsities=None,
+                 layouts: Optional[Sequence[Sequence[int]]] = None, dense: Optional[bool] = None):
+        super().__init__(config, layer_idx)
+        self.num_heads = config.num_attention_heads
+        self.num_key_value_heads = config.num_key_value_heads
+        self.pattern_name = _get(config, "sparse_attention_pattern", "local")
+        requested = backend_name or _get(config, "sparse_attention_backend", "auto")
+        if requested not in ("auto", "cuda_sm100"):
+            raise ValueError(f"backend {requested!r} unavailable: this package provides 'cuda_sm100' only")
+        self.backend_name = "cuda_sm100"
+        self.window_size = window_size or _get(config, "sparse_attention_window_size", 512)
+        self.block_size = block_size or _get(config, "sparse_attention_block_size", 64)
+        self.top_k = _get(config, "sparse_attention_top_k", 128)
+        keep_ratio = _get(config, "sparse_attention_keep_ratio", None)
+        gs = normalize_group_sparsities(group_sparsities)
+        if layouts is None:
+            lay_cfg = _get(config, "sparse_attention_layer_layouts", None)
+            if lay_cfg is not None and layer_idx < len(lay_cfg):
+                layouts = lay_cfg[layer_idx]
+                if layouts is None and dense is None:
+                    dense = True
+        if gs is None and layouts is None:
+            lgs = normalize_layer_group_sparsities(_get(config, "sparse_attention_layer_group_sparsities", None))
+            if lgs is not None and layer_idx < len(lgs):
+                gs = lgs[layer_idx]
+        if gs is None and layouts is None:
+            gs = normalize_group_sparsities(_get(config, "sparse_attention_group_sparsities", None))
+        self.group_sparsities = gs
+        self.keep_ratio = None if gs is not None else keep_ratio
+        self.dense = bool(dense) or self.pattern_name == "dense"
+        self.sparse_backend = CudaSm100Backend()
+        self.sparse_pattern = self._make_pattern(layouts)
+        self.last_pattern_stats: Optional[dict] = None
+        self.collect_pattern_stats = True
+
+    @property
+    def actual_backend(self) -> str:
+        return self.sparse_backend.actual_backend
+
+    def _make_pattern(self, layouts) -> SparsePattern:
+        H, Hkv = self.num_heads, self.num_key_value_heads
+        if self.dense:
+            return DenseCausalPattern()
+        if layouts is not None:
+            return BigBirdKeepRatioPattern(layouts=[tuple(l) for l in layouts], n_heads=H)
+        if self.pattern_name == "bigbird":
+            if self.group_sparsities is not None:
+                return BigBirdKeepRatioPattern(group_sparsities=self.group_sparsities, n_heads=H, n_kv_heads=Hkv)
+            if self.keep_ratio is not None:
+                return BigBirdKeepRatioPattern(keep_ratio=self.keep_ratio, n_heads=H, n_kv_heads=Hkv)
+            return BigBirdPattern(top_k=self.top_k, n_heads=H)
+        return LocalWindowPattern(window_size=self.window_size, block_size=self.block_size, materialize_mask=False)
+
+    def forward(self, hidden_states: torch.Tensor, position_embeddings: tuple[torch.Tensor, torch.Tensor],
+                attention_mask: Optional[torch.Tensor] = None, past_key_values: Optional[Cache] = None, **kwargs):
+        if kwargs.get("output_attentions", False):
+            raise NotImplementedError("Sparse kernel path does not return attention weights.")
+        input_shape = hidden_states.shape[:-1]
+        hidden_shape = (*input_shape, -1, self.head_dim)
+        q = self.q_norm(self.q_proj(hidden_states).view(hidden_shape)).transpose(1, 2)
+        k = self.k_norm(self.k_proj(hidden_states).view(hidden_shape)).transpose(1, 2)
+        v = self.v_proj(hidden_states).view(hidden_shape).transpose(1, 2)
+        cos, sin = position_embeddings
+        q, k = apply_rotary_pos_emb(q, k, cos, sin)
+        if past_key_values is not None:
+            k, v = past_key_values.update(k, v, self.layer_idx)
+        pattern = self.sparse_pattern.build(q, k, causal=True)
+        if self.collect_pattern_stats:
+            kr = pattern.keep_ratio
+            self.last_pattern_stats = {"keep_ratio": float(kr), "sparsity": 1.0 - float(kr)}
+        out = self.sparse_backend.forward(q, k, v, pattern)
+        out = out.transpose(1, 2).reshape(*input_shape, -1).contiguous()
+        return self.o_proj(out), None
+
+
+def build_sparse_attention_from_dense(attention: nn.Module, **kw) -> Qwen3SparseKernelAttention:
+    """modeling_sparse_qwen3.py:320-344: same weights, sparse core."""
+    target_dtype = kw.pop("target_dtype", None)
+    sa = Qwen3SparseKernelAttention(attention.config, layer_idx=attention.layer_idx, **kw)
+    sa.load_state_dict(attention.state_dict(), strict=False)
+    sa.to(device=attention.q_proj.weight.device, dtype=target_dtype or attention.q_proj.weight.dtype)
+    return sa
+
+
+def replace_qwen3_attention_with_sparse(model: nn.Module, *, block_size: int = 64, group_sparsities=None,
+                                        layer_group_sparsities=None, layer_layouts=None,
+                                        target_dtype=None, **kw) -> nn.Module:
+    """modeling_sparse_qwen3.py:347-406. ``layer_layouts[i]`` (a list of per-group
+    (bs, g, w, r) layouts, or None for a dense layer) overrides the sparsities."""
+    base = model.model if hasattr(model, "model") and hasattr(model.model, "layers") else model
+    if not hasattr(base, "layers"):
+        raise TypeError("Expected a Qwen3 decoder model with a `.layers` attribute.")
+    gs = normalize_group_sparsities(group_sparsities)
+    lgs = normalize_layer_group_sparsities(layer_group_sparsities)
+    if lgs is not None and len(lgs) > len(base.layers):
+        raise ValueError("layer_group_sparsities has more entries than there are decoder layers.")
+    if layer_layouts is not None and len(layer_layouts) > len(base.layers):
+        raise ValueError("layer_layouts has more entries than there are decoder layers.")
+    for layer in base.layers:
+        li = layer.self_attn.layer_idx
+        args = dict(kw, block_size=block_size, target_dtype=target_dtype)
+        if layer_layouts is not None and li < len(layer_layouts):
+            if layer_layouts[li] is None:
+                args["dense"] = True
+            else:
+                args["layouts"] = layer_layouts[li]
+        else:
+            layer_gs = lgs[li] if lgs is not None and li < len(lgs) else None
+            args["group_sparsities"] = layer_gs if layer_gs is not None else gs
+        layer.self_attn = build_sparse_attention_from_dense(layer.self_attn, **args)
+    return model
+
+
+class Qwen3SparseKernelForCausalLM(Qwen3ForCausalLM):
+    """modeling_sparse_qwen3.py:470-484: every layer's attention is replaced at construction."""
+
+    def __init__(self, config: Qwen3Config, *, group_sparsities=None, layer_group_sparsities=None,
+                 layer_layouts=None):
+        if not hasattr(config, "_attn_implementation") or config._attn_implementation is None:
+            config._attn_implementation = "eager"
+        super().__init__(config)
+        replace_qwen3_attention_with_sparse(
+            self.model, block_size=_get(config, "sparse_attention_block_size", 64),
+            group_sparsities=group_sparsities if group_sparsities is not None
+            else _get(config, "sparse_attention_group_sparsities", None),
+            layer_group_sparsities=layer_group_sparsities if layer_group_sparsities is not None
+            else _get(config, "sparse_attention_layer_group_sparsities", None),
+            layer_layouts=layer_layouts if layer_layouts is not None
+            else _get(config, "sparse_attention_layer_layouts", None))
+
+
+class PreallocatedLayer(DynamicLayer):
+    """KV layer with a fixed [B, Hkv, capacity, D] buffer; ``update`` writes the new
+    tokens in place and returns [:, :, :T] views (no per-step concatenation)."""
+
+    def __init__(self, capacity: int):
+        super().__init__()
+        self.capacity = capacity
+        self.length = 0
+
+    def lazy_initialization(self, key_states, value_states):
+        self.dtype, self.device = key_states.dtype, key_states.device
+        B, H, _, D = key_states.shape
+        self.k_buf = torch.empty(B, H, self.capacity, D, dtype=self.dtype, device=self.device)
+        self.v_buf = torch.empty(B, H, self.capacity, D, dtype=self.dtype, device=self.device)
+        self.keys, self.values = self.k_buf[:, :, :0], self.v_buf[:, :, :0]
+        self.is_initialized = True
+
+    def update(self, key_states, value_states, *args, **kwargs):
+        if not self.is_initialized:
+            self.lazy_initialization(key_states, value_states)
+        n = key_states.shape[-2]
+        if self.length + n > self.capacity:
+            raise RuntimeError(f"KV cache capacity {self.capacity} exceeded")
+        self.k_buf[:, :, self.length:self.length + n].copy_(key_states)
+        self.v_buf[:, :, self.length:self.length + n].copy_(value_states)
+        self.length += n
+        self.keys = self.k_buf[:, :, :self.length]
+        self.values = self.v_buf[:, :, :self.length]
+        return self.keys, self.values
+
+    def get_seq_length(self) -> int:
+        return self.length
+
+    def get_max_cache_shape(self) -> int:
+        return self.capacity
+
+    def reset(self) -> None:
+        self.length = 0
+        if self.is_initialized:
+            self.keys, self.values = self.k_buf[:, :, :0], self.v_buf[:, :, :0]
+
+
+class PreallocatedKVCache(Cache):
+    """transformers Cache of ``PreallocatedLayer`` (one per decoder layer)."""
+
+    def __init__(self, num_layers: int, capacity: int):
+        super().__init__(layers=[PreallocatedLayer(capacity) for _ in range(num_layers)])
+
+
+__all__ = [
+    "Qwen3SparseKernelAttention", "replace_qwen3_attention_with_sparse", "build_sparse_attention_from_dense",
+    "Qwen3SparseKernelForCausalLM", "PreallocatedKVCache", "PreallocatedLayer", "build_layer_block_experiments",
+    "normalize_group_sparsities", "normalize_layer_group_sparsities",
+]
