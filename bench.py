@@ -229,6 +229,86 @@ def time_decode(device) -> dict:
             "note": "2 launches per step (split + combine); L2 flushed between steps"}
 
 
+
+def time_qwen3_decode(device, layers=36, batch=32, ctx=32768, steps=256, chunk=1024, sparse_layers=18,
+                      seed=0) -> dict:
+    """Config 4: random-init Qwen3-4B architecture (hidden 2560, 36 layers, 32/8 heads,
+    head_dim 128, SwiGLU 9728, vocab 151936, RoPE 1e6, weights N(0,0.02)) in bf16,
+    batch 32, KV cache prefilled (chunked) from 32768 uniform-random token ids,
+    BigBird (64, 2, 4, 2) in layers 0..17, layers 18..35 dense; then `steps`
+    greedy decode steps. Arm "sparse": this package's hook (sparse layers on the
+    split-KV decode kernel, dense layers on PyTorch SDPA). Arm "dense": the same
+    model and cache with every layer on PyTorch SDPA (the dense FlashAttention
+    comparator). Both arms decode from the same prefilled cache (decode cost does
+    not depend on the cached values). Timing: CUDA events around the decode
+    loop (host overhead of the HF model included, per-step argmax on device)."""
+    from transformers import Qwen3Config, Qwen3ForCausalLM
+    from sparseattentioninfer_b200 import qwen3 as sq
+    sq.register_attention_implementation()
+    cfg = Qwen3Config(vocab_size=151936, hidden_size=2560, intermediate_size=9728, num_hidden_layers=layers,
+                      num_attention_heads=32, num_key_value_heads=8, head_dim=128, rope_theta=1e6,
+                      max_position_embeddings=ctx + steps + 16, tie_word_embeddings=True, initializer_range=0.02)
+    cfg._attn_implementation = "cuda_sm100"
+    cfg.sparse_attention_dense_impl = "sdpa"
+    torch.manual_seed(seed)
+    with torch.device(device):
+        model = Qwen3ForCausalLM(cfg).to(torch.bfloat16).eval()
+    layer_layouts = [[(64, 2, 4, 2)]] * sparse_layers + [None] * (layers - sparse_layers)
+    sq.replace_qwen3_attention_with_sparse(model, layer_layouts=layer_layouts)
+    for l in model.model.layers:
+        l.self_attn.collect_pattern_stats = False
+    cache = sq.PreallocatedKVCache(layers, ctx + steps + 8)
+    g = torch.Generator(device=device).manual_seed(seed + 1)
+    ids = torch.randint(0, cfg.vocab_size, (batch, ctx), generator=g, device=device)
+    out = {"workload": f"qwen3_4b_arch_b{batch}_ctx{ctx}_bigbird64_2_4_2_layers0-{sparse_layers - 1}",
+           "layers": layers, "batch": batch, "ctx": ctx, "steps": steps}
+    with torch.no_grad():
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        logits = None
+        for c in range(0, ctx, chunk):
+            logits = model(ids[:, c:c + chunk], past_key_values=cache, use_cache=True, logits_to_keep=1).logits
+        torch.cuda.synchronize()
+        out["prefill_s"] = time.perf_counter() - t0
+        first = logits[:, -1].argmax(-1, keepdim=True)
+
+        def decode(n):
+            tok = first
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            for i in range(n + 3):
+                if i == 3:
+                    e0.record()
+                tok = model(tok, past_key_values=cache, use_cache=True, logits_to_keep=1).logits[:, -1].argmax(
+                    -1, keepdim=True)
+            e1.record()
+            torch.cuda.synchronize()
+            return e0.elapsed_time(e1) / 1e3
+
+        def rewind():
+            for layer in cache.layers:
+                layer.length = ctx
+
+        # Each arm runs twice over the same 256 lengths and the second pass is
+        # timed: PyTorch SDPA (cuDNN) builds an execution plan per new KV length
+        # (~25 ms of host time), which the warm pass caches for both arms.
+        decode(steps)
+        rewind()
+        t_sparse = decode(steps)
+        rewind()
+        for l in model.model.layers:
+            l.self_attn.set_dense(True, "sdpa")
+        decode(steps)
+        rewind()
+        t_dense = decode(steps)
+    out["sparse_tok_s"] = batch * steps / t_sparse
+    out["dense_tok_s"] = batch * steps / t_dense
+    out["sparse_ms_per_step"] = t_sparse / steps * 1e3
+    out["dense_ms_per_step"] = t_dense / steps * 1e3
+    out["speedup_vs_dense_sdpa"] = t_dense / t_sparse
+    del model, cache
+    torch.cuda.empty_cache()
+    return out
+
 def run_ours(args) -> None:
     world, rank, local = dist_env()
     if world > 1:
@@ -349,6 +429,15 @@ def run_ours(args) -> None:
         line["decode"]["traffic"] = traffic_from_profile("decode_qwen3_4b_layer_ncu.txt")
     except Exception as e:  # noqa: BLE001
         line["decode"] = {"error": repr(e)}
+    if args.model != "off" and world == 1:
+        del q, k, v, out, md
+        torch.cuda.empty_cache()
+        try:
+            line["model_decode"] = time_qwen3_decode(device, layers=args.model_layers, ctx=args.model_ctx,
+                                                     sparse_layers=args.model_layers // 2,
+                                                     steps=args.model_steps)
+        except Exception as e:  # noqa: BLE001
+            line["model_decode"] = {"error": repr(e)[:300]}
     if world == 1 and not args.no_cpu_baseline:
         threads = os.cpu_count() or 1
         rate, done, wall = cpu_sample(bitmap.cpu(), args.cpu_seconds, 64, threads)
@@ -368,6 +457,11 @@ def main() -> None:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--model", choices=["on", "off"], default="on",
+                    help="also time the Qwen3-4B-shaped sparse model decode (config 4)")
+    ap.add_argument("--model-layers", type=int, default=36)
+    ap.add_argument("--model-ctx", type=int, default=32768)
+    ap.add_argument("--model-steps", type=int, default=256)
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -24,7 +24,6 @@ the ``torch.cat`` growth of DynamicCache (one O(T) copy per step per layer).
 """
 from __future__ import annotations
 
-from collections import OrderedDict
 from typing import Any, Optional, Sequence
 
 import torch
@@ -41,6 +40,30 @@ from .patterns import (
     LocalWindowPattern,
     SparsePattern,
 )
+
+
+ATTN_IMPLEMENTATION = "cuda_sm100"
+
+
+def _no_mask(*args, **kwargs):
+    """The kernels apply causality (and padding is unsupported, as in the
+    reference hook): no [B, 1, T_q, T_k] mask is materialised."""
+    return None
+
+
+def _attention_interface(module, query, key, value, attention_mask, **kwargs):
+    raise RuntimeError("layers using the cuda_sm100 implementation must be Qwen3SparseKernelAttention")
+
+
+def register_attention_implementation() -> str:
+    """Register ``cuda_sm100`` with transformers' attention and mask interfaces so a
+    model config can name it (``config._attn_implementation = "cuda_sm100"``):
+    mask creation is then skipped entirely."""
+    from transformers.masking_utils import ALL_MASK_ATTENTION_FUNCTIONS
+    from transformers.modeling_utils import ALL_ATTENTION_FUNCTIONS
+    ALL_MASK_ATTENTION_FUNCTIONS.register(ATTN_IMPLEMENTATION, _no_mask)
+    ALL_ATTENTION_FUNCTIONS.register(ATTN_IMPLEMENTATION, _attention_interface)
+    return ATTN_IMPLEMENTATION
 
 
 def _get(config, name: str, default):
@@ -82,18 +105,6 @@ def build_layer_block_experiments(*, num_layers: int, num_groups: int, layer_spa
     return exps
 
 
-class _LRU(OrderedDict):
-    def __init__(self, cap: int):
-        super().__init__()
-        self.cap = cap
-
-    def put(self, k, v):
-        self[k] = v
-        self.move_to_end(k)
-        while len(self) > self.cap:
-            self.popitem(last=False)
-
-
 class Qwen3SparseKernelAttention(Qwen3Attention):
     """HF Qwen3 attention with the attention core replaced by the cuda_sm100 backend."""
 
@@ -132,10 +143,22 @@ class Qwen3SparseKernelAttention(Qwen3Attention):
         self.sparse_pattern = self._make_pattern(layouts)
         self.last_pattern_stats: Optional[dict] = None
         self.collect_pattern_stats = True
+        # Dense layers run the cuda_sm100 kernel over a dense causal CSR; "sdpa"
+        # selects PyTorch SDPA (library FlashAttention / cuDNN), the comparator
+        # the reference's benchmarks call the dense path.
+        self.dense_impl = _get(config, "sparse_attention_dense_impl", "cuda_sm100")
 
     @property
     def actual_backend(self) -> str:
         return self.sparse_backend.actual_backend
+
+    def set_dense(self, dense: bool = True, impl: Optional[str] = None) -> None:
+        """Switch this layer to full causal attention (or back to its pattern)."""
+        if impl is not None:
+            self.dense_impl = impl
+        if dense:
+            self.dense = True
+            self.sparse_pattern = DenseCausalPattern()
 
     def _make_pattern(self, layouts) -> SparsePattern:
         H, Hkv = self.num_heads, self.num_key_value_heads
@@ -164,6 +187,13 @@ class Qwen3SparseKernelAttention(Qwen3Attention):
         q, k = apply_rotary_pos_emb(q, k, cos, sin)
         if past_key_values is not None:
             k, v = past_key_values.update(k, v, self.layer_idx)
+        if self.dense and self.dense_impl == "sdpa" and q.shape[2] in (1, k.shape[2]):
+            # (SDPA aligns its causal mask top-left, so chunked prefill, 1 < T_q < T_k,
+            # stays on the cuda_sm100 kernel, whose mask is bottom-right aligned.)
+            T_q = q.shape[2]
+            out = torch.nn.functional.scaled_dot_product_attention(q, k, v, is_causal=T_q > 1, enable_gqa=True)
+            out = out.transpose(1, 2).reshape(*input_shape, -1).contiguous()
+            return self.o_proj(out), None
         pattern = self.sparse_pattern.build(q, k, causal=True)
         if self.collect_pattern_stats:
             kr = pattern.keep_ratio
