@@ -236,10 +236,11 @@ def time_qwen3_decode(device, layers=36, batch=32, ctx=32768, steps=256, chunk=1
     head_dim 128, SwiGLU 9728, vocab 151936, RoPE 1e6, weights N(0,0.02)) in bf16,
     batch 32, KV cache prefilled (chunked) from 32768 uniform-random token ids,
     BigBird (64, 2, 4, 2) in layers 0..17, layers 18..35 dense; then `steps`
-    greedy decode steps. Arm "sparse": this package's hook (sparse layers on the
-    split-KV decode kernel, dense layers on PyTorch SDPA). Arm "dense": the same
-    model and cache with every layer on PyTorch SDPA (the dense FlashAttention
-    comparator). Both arms decode from the same prefilled cache (decode cost does
+    greedy decode steps through the lean runner (runtime.Qwen3DecodeRunner; the
+    prefill runs through the HF model with the hook). Arm "sparse": sparse layers
+    on the split-KV decode kernel, dense layers on PyTorch SDPA; arm
+    "sparse_own_dense": dense layers on the decode kernel too; arm "dense": every
+    layer on PyTorch SDPA (the dense FlashAttention comparator). Both arms decode from the same prefilled cache (decode cost does
     not depend on the cached values). Timing: CUDA events around the decode
     loop (host overhead of the HF model included, per-step argmax on device)."""
     from transformers import Qwen3Config, Qwen3ForCausalLM
@@ -272,14 +273,15 @@ def time_qwen3_decode(device, layers=36, batch=32, ctx=32768, steps=256, chunk=1
         out["prefill_s"] = time.perf_counter() - t0
         first = logits[:, -1].argmax(-1, keepdim=True)
 
-        def decode(n):
+        from sparseattentioninfer_b200.runtime import Qwen3DecodeRunner
+
+        def decode(runner, n):
             tok = first
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             for i in range(n + 3):
                 if i == 3:
                     e0.record()
-                tok = model(tok, past_key_values=cache, use_cache=True, logits_to_keep=1).logits[:, -1].argmax(
-                    -1, keepdim=True)
+                tok = runner.step(tok)
             e1.record()
             torch.cuda.synchronize()
             return e0.elapsed_time(e1) / 1e3
@@ -288,18 +290,20 @@ def time_qwen3_decode(device, layers=36, batch=32, ctx=32768, steps=256, chunk=1
             for layer in cache.layers:
                 layer.length = ctx
 
-        # Each arm runs twice over the same 256 lengths and the second pass is
-        # timed: PyTorch SDPA (cuDNN) builds an execution plan per new KV length
-        # (~25 ms of host time), which the warm pass caches for both arms.
-        decode(steps)
-        rewind()
-        t_sparse = decode(steps)
-        rewind()
-        for l in model.model.layers:
-            l.self_attn.set_dense(True, "sdpa")
-        decode(steps)
-        rewind()
-        t_dense = decode(steps)
+        # Each arm runs twice over the same lengths and the second pass is timed:
+        # PyTorch SDPA (cuDNN) builds an execution plan per new KV length (~25 ms
+        # of host time), which the warm pass caches, for both arms alike.
+        arms = {"sparse": Qwen3DecodeRunner(model, cache, layer_layouts, dense_impl="sdpa"),
+                "sparse_own_dense": Qwen3DecodeRunner(model, cache, layer_layouts, dense_impl="cuda_sm100"),
+                "dense": Qwen3DecodeRunner(model, cache, [None] * layers, dense_impl="sdpa")}
+        times = {}
+        for name, runner in arms.items():
+            rewind()
+            decode(runner, steps)
+            rewind()
+            times[name] = decode(runner, steps)
+        t_sparse, t_dense = times["sparse"], times["dense"]
+        out["sparse_own_dense_tok_s"] = batch * steps / times["sparse_own_dense"]
     out["sparse_tok_s"] = batch * steps / t_sparse
     out["dense_tok_s"] = batch * steps / t_dense
     out["sparse_ms_per_step"] = t_sparse / steps * 1e3

@@ -106,3 +106,30 @@ def test_sparse_qwen3_matches_oracle_prefill_and_decode(monkeypatch):
     assert max(errs) <= 0.1, errs
     assert min(agree) >= 0.95, agree
     assert sparse.model.layers[0].self_attn.actual_backend == "cuda_sm100"
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dense_impl", ["sdpa", "cuda_sm100"])
+def test_decode_runner_matches_hf_hook(dense_impl):
+    """The lean decode runner computes the same decode steps as the HF model with the hook."""
+    from sparseattentioninfer_b200.runtime import Qwen3DecodeRunner
+    torch.manual_seed(0)
+    cfg = tiny_config()
+    model = Qwen3ForCausalLM(cfg).to("cuda", torch.bfloat16).eval()
+    layer_layouts = [[(64, 1, 2, 1), (64, 2, 3, 0)], None, [(64, 1, 1, 2)]]
+    sq.replace_qwen3_attention_with_sparse(model, layer_layouts=layer_layouts)
+    ids = torch.randint(0, cfg.vocab_size, (2, 333), generator=torch.Generator().manual_seed(3)).cuda()
+    ca, cb = sq.PreallocatedKVCache(3, 400), sq.PreallocatedKVCache(3, 400)
+    with torch.no_grad():
+        la = model(ids, past_key_values=ca, use_cache=True).logits
+        model(ids, past_key_values=cb, use_cache=True)
+        runner = Qwen3DecodeRunner(model, cb, layer_layouts, dense_impl=dense_impl)
+        tok = la[:, -1].argmax(-1, keepdim=True)
+        tb = tok
+        for _ in range(4):
+            lhf = model(tok, past_key_values=ca, use_cache=True).logits[:, -1].float()
+            tb_next, lr = runner.step(tb, return_logits=True)
+            assert (lr.float() - lhf).abs().max().item() <= 0.05
+            tok = lhf.argmax(-1, keepdim=True)
+            tb = tok  # feed both the same token
+    assert cb.get_seq_length() == ca.get_seq_length() == 337
