@@ -18,6 +18,10 @@ int sa_cuda_check(cudaError_t e, const char* what);
 int sa_num_sms();
 // Device address of the library-wide device error word (cudaGetSymbolAddress).
 int32_t* sa_device_error_ptr();
+// 4-D bf16 TMA map over [B, H, T, D] with element strides {b, h, t}: box (64, box_rows, 1, 1),
+// SWIZZLE_128B, out-of-range elements read as zero.
+int sa_make_map(CUtensorMap* m, const void* base, int B, int H, int T, int D, const int64_t strides[3],
+                int box_rows, const char* name);
 
 #define SA_CHECK_CUDA(call)                                   \
   do {                                                        \

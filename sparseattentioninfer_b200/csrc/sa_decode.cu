@@ -4,122 +4,139 @@
 // (kernels/triton/universal_sparse_attn.py:45-160 with Q_OFFSET = T_k, :84-89),
 // which spends a 1-row query block per (b, q-head) and re-reads K/V per head.
 // Here one CTA serves a (b, kv-head, split): it reads each retained KV block of
-// the group once for all Hq/Hkv query heads. The reference draws different
+// the group once for all G = Hq/Hkv query heads. The reference draws different
 // random blocks per query head (bigbird_pattern.py:23-41), so the CTA first
 // builds the sorted union of the group's CSR rows in shared memory (a per-block
 // head bitmask, filled in parallel and compacted), then takes its contiguous
 // share of the union.
-// Memory path: a ring of kDecStages stages of up to 64 keys of K and V, filled
-// by untiled bulk copies (cp.async.bulk, mbarrier completion) issued by one
-// thread, so a whole stage is in flight per instruction; four warps consume
-// each stage from shared memory (D/8 lanes per key row, 16-byte reads).
-// Statistics in fp32 (log2 domain). A second kernel merges the splits
-// (log-sum-exp) and writes bf16.
+//
+// Pipeline: a producer warp streams stages of up to 64 keys of K and V with TMA
+// (4-D tensor maps, SWIZZLE_128B, zero fill past T_k) into a 3-stage ring; four
+// consumer warps take 16 keys each and do both products on the tensor cores
+// with mma.sync m16n8k16 (bf16 in, fp32 accumulate): the group's G query rows
+// are padded to the 16-row A operand, K fragments come from ldmatrix on the
+// swizzled rows, V fragments from ldmatrix.trans, and P goes from the S
+// accumulators straight into the A operand of PV. Online softmax per warp in
+// fp32 (log2 domain); warps and splits are merged by log-sum-exp (a second tiny
+// kernel when n_split > 1; the split kernel writes bf16 directly otherwise).
 #include <cstring>
 
 #include "sa_common.cuh"
 
 namespace sa {
 
-constexpr int kDecThreads = 128;
-constexpr int kDecWarps = kDecThreads / 32;
+constexpr int kDecConsumers = 4;                  // consumer warps
+constexpr int kDecThreads = 32 * (kDecConsumers + 1);
 constexpr int kDecStages = 3;
-constexpr int kDecChunk = 64;        // keys per stage
+constexpr int kDecChunk = 64;        // max keys per stage
 constexpr int kMaxUnion = 2048;      // union entries per (b, kv head)
 constexpr int kMaxNkbWords = 2048;   // membership bytes packed 4 per word: NKB <= 8192
 
 struct DecodeParams {
+  CUtensorMap tm_k;
+  CUtensorMap tm_v;
   const __nv_bfloat16* q;
-  const __nv_bfloat16* k;
-  const __nv_bfloat16* v;
-  int64_t q_sb, q_sh, k_sb, k_sh, k_st, v_sb, v_sh, v_st;
+  int64_t q_sb, q_sh;
   const int32_t* pairs;
   const int32_t* offsets;
   int32_t pairs_stride;
-  int32_t B, Hq, Hkv, T_k, bs, n_split;
+  int32_t B, Hq, Hkv, T_k, bs, n_split, chk;
   float scale_log2;
   float* part_o;   // [B, Hq, n_split, D]
   float* part_ml;  // [B, Hq, n_split, 2]
+  __nv_bfloat16* out;  // written directly when n_split == 1
+  int64_t o_sb, o_sh;
   int32_t* err;
 };
 
 template <int D>
 struct DecodeCfg {
-  static constexpr int kStageBytes = kDecChunk * D * 2;  // K (or V) of one stage
-  static constexpr int kSmemBytes = 2 * kDecStages * kStageBytes + 128;
+  static constexpr int kRegions = D / 64;
+  static constexpr int kHalfBytes = kDecChunk * D * 2;          // K (or V) of one stage
+  static constexpr int kStageBytes = 2 * kHalfBytes;
+  static constexpr int kSmemBytes = kDecStages * kStageBytes;
 };
 
-__device__ __forceinline__ void bf16x8_to_f32(const uint4 u, float (&f)[8]) {
-  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    float2 t = __bfloat1622float2(h[i]);
-    f[2 * i] = t.x;
-    f[2 * i + 1] = t.y;
-  }
-}
+#ifdef SA_PHASE_TRACE
+__device__ unsigned long long g_dec_trace[4096 * 4];
+#define DEC_TRACE(slot)                                                                                   \
+  do {                                                                                                    \
+    const int cta_ = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);                       \
+    if (threadIdx.x == 0 && cta_ < 4096) {                                                                \
+      unsigned long long t_;                                                                              \
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));                                             \
+      g_dec_trace[cta_ * 4 + (slot)] = t_;                                                                \
+    }                                                                                                     \
+  } while (0)
+#else
+#define DEC_TRACE(slot) \
+  do {                  \
+  } while (0)
+#endif
 
-// Issue the bulk copies of one stage (rows [key0, key0+rows) of K and V).
-template <int D>
-__device__ __forceinline__ void issue_stage(const DecodeParams& p, int b, int kvh, int key0, int rows,
-                                            uint32_t sk, uint32_t sv, uint32_t bar) {
-  constexpr uint32_t kRow = D * 2;
-  if (rows <= 0) {
-    mbar_arrive(bar);
-    return;
-  }
-  mbar_arrive_expect_tx(bar, 2u * rows * kRow);
-  const __nv_bfloat16* kp = p.k + (int64_t)b * p.k_sb + (int64_t)kvh * p.k_sh + (int64_t)key0 * p.k_st;
-  const __nv_bfloat16* vp = p.v + (int64_t)b * p.v_sb + (int64_t)kvh * p.v_sh + (int64_t)key0 * p.v_st;
-  if (p.k_st == D) {
-    bulk_load(sk, kp, rows * kRow, bar);
-  } else {
-    for (int r = 0; r < rows; ++r) bulk_load(sk + r * kRow, kp + (int64_t)r * p.k_st, kRow, bar);
-  }
-  if (p.v_st == D) {
-    bulk_load(sv, vp, rows * kRow, bar);
-  } else {
-    for (int r = 0; r < rows; ++r) bulk_load(sv + r * kRow, vp + (int64_t)r * p.v_st, kRow, bar);
-  }
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+// D = A(16x16, row) * B(16x8, col) + D, bf16 inputs, fp32 accumulators.
+__device__ __forceinline__ void mma_bf16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+// Shared address of 16-byte chunk `c` (of 8 per 128-byte row) of row `r` in a
+// SWIZZLE_128B region (1024-byte aligned): TMA stored it XOR-permuted by r%8.
+__device__ __forceinline__ uint32_t sw128(uint32_t region, int r, int c) {
+  return region + r * 128 + ((c ^ (r & 7)) << 4);
 }
 
 template <int D, int G>
-__global__ void __launch_bounds__(kDecThreads) decode_split_kernel(const DecodeParams p) {
+__global__ void __launch_bounds__(kDecThreads) decode_split_kernel(const __grid_constant__ DecodeParams p) {
   using Cfg = DecodeCfg<D>;
-  constexpr int LPK = D / 8;          // lanes per key row (16 B each)
-  constexpr int KPW = 32 / LPK;       // key rows per warp instruction
-  constexpr int KPWARP = kDecChunk / kDecWarps;  // keys of a stage per warp
-  constexpr int IT = KPWARP / KPW;    // warp instructions per stage
+  constexpr int R = Cfg::kRegions;
+  constexpr int NT = D / 8;  // n-tiles of the PV product
   __shared__ int s_kb[kMaxUnion];
   __shared__ uint8_t s_hm[kMaxUnion];
-  __shared__ int s_warp_cnt[kDecWarps + 1];
+  __shared__ int s_warp_cnt[kDecThreads / 32 + 1];
   __shared__ __align__(8) uint64_t bar_full[kDecStages], bar_empty[kDecStages];
-  __shared__ float s_m[kDecWarps][G], s_l[kDecWarps][G];
+  __shared__ float s_m[kDecConsumers][8], s_l[kDecConsumers][8];
   __shared__ int abort_flag;
-  extern __shared__ __align__(128) uint8_t dsmem[];
-  const uint32_t sbase = (smem_u32(dsmem) + 127u) & ~127u;
+  extern __shared__ __align__(1024) uint8_t dsmem[];
+  const uint32_t sbase = smem_u32(dsmem);
   // The stage ring is free before the first copy and after the drain: it holds
   // the membership words first and the per-warp partial outputs last.
-  uint32_t* s_memb = reinterpret_cast<uint32_t*>(dsmem + (sbase - smem_u32(dsmem)));
-  float(*s_o)[G][D] = reinterpret_cast<float(*)[G][D]>(dsmem + (sbase - smem_u32(dsmem)));
-  static_assert(kMaxNkbWords * 4 <= 2 * kDecStages * DecodeCfg<D>::kStageBytes, "ring too small");
-  static_assert(kDecWarps * G * D * 4 <= 2 * kDecStages * DecodeCfg<D>::kStageBytes, "ring too small");
+  uint32_t* s_memb = reinterpret_cast<uint32_t*>(dsmem);
+  float(*s_o)[8][D] = reinterpret_cast<float(*)[8][D]>(dsmem);
+  static_assert(kMaxNkbWords * 4 <= kDecStages * Cfg::kStageBytes, "ring too small");
+  static_assert(kDecConsumers * 8 * D * 4 <= kDecStages * Cfg::kStageBytes, "ring too small");
+  static_assert(G <= 8, "at most 8 query heads per KV group");
 
   const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int h0 = kvh * G;
   const int nkb = (p.T_k + p.bs - 1) / p.bs;
   const int nwords = (nkb + 3) >> 2;
+  DEC_TRACE(0);
 
   if (tid == 0) {
+    if (sbase & 1023u) record_error(p.err, SA_DEV_ERR_INDEX);
     for (int i = 0; i < kDecStages; ++i) {
       mbar_init(smem_u32(&bar_full[i]), 1);
-      mbar_init(smem_u32(&bar_empty[i]), kDecWarps);
+      mbar_init(smem_u32(&bar_empty[i]), kDecConsumers);
     }
     abort_flag = 0;
     fence_mbar_init();
   }
-  if (nwords > kMaxNkbWords) {  // block-uniform
+  if (nwords > kMaxNkbWords || (sbase & 1023u)) {  // block-uniform
     if (tid == 0) record_error(p.err, SA_DEV_ERR_INDEX);
     return;
   }
@@ -154,12 +171,12 @@ __global__ void __launch_bounds__(kDecThreads) decode_split_kernel(const DecodeP
   __syncthreads();
   if (tid == 0) {
     int acc = 0;
-    for (int w = 0; w < kDecWarps; ++w) {
+    for (int w = 0; w < kDecThreads / 32; ++w) {
       const int c = s_warp_cnt[w];
       s_warp_cnt[w] = acc;
       acc += c;
     }
-    s_warp_cnt[kDecWarps] = acc;
+    s_warp_cnt[kDecThreads / 32] = acc;
   }
   __syncthreads();
   {
@@ -178,170 +195,167 @@ __global__ void __launch_bounds__(kDecThreads) decode_split_kernel(const DecodeP
     }
   }
   __syncthreads();  // membership words no longer needed: the ring may be filled
-  const int U = min(s_warp_cnt[kDecWarps], kMaxUnion);
-  if (tid == 0 && s_warp_cnt[kDecWarps] > kMaxUnion) record_error(p.err, SA_DEV_ERR_INDEX);
+  DEC_TRACE(1);
+  const int U = min(s_warp_cnt[kDecThreads / 32], kMaxUnion);
+  if (tid == 0 && s_warp_cnt[kDecThreads / 32] > kMaxUnion) record_error(p.err, SA_DEV_ERR_INDEX);
   const int e_begin = (int)(((int64_t)U * split) / p.n_split);
   const int e_end = (int)(((int64_t)U * (split + 1)) / p.n_split);
-  const int chk = min(p.bs, kDecChunk);      // keys per stage
-  const int nsub = p.bs > kDecChunk ? p.bs / kDecChunk : 1;
-  const int nst = (e_end - e_begin) * nsub;  // stages of this split
+  const int chk = p.chk;                                    // keys per stage (= TMA box rows)
+  const int nsub = p.bs > chk ? p.bs / chk : 1;
+  const int nst = (e_end - e_begin) * nsub;                 // stages of this split
+  volatile int* abort_v = &abort_flag;
 
   auto stage_key0 = [&](int i) { return s_kb[e_begin + i / nsub] * p.bs + (i % nsub) * chk; };
-  auto stage_rows = [&](int i) { return max(0, min(chk, p.T_k - stage_key0(i))); };
-  auto sK = [&](int slot) { return sbase + slot * 2 * Cfg::kStageBytes; };
-  auto sV = [&](int slot) { return sbase + slot * 2 * Cfg::kStageBytes + Cfg::kStageBytes; };
 
-  if (tid == 0) {
-    // generic-proxy writes (membership words) precede async-proxy writes here
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    for (int i = 0; i < min(nst, kDecStages); ++i)
-      issue_stage<D>(p, b, kvh, stage_key0(i), stage_rows(i), sK(i), sV(i), smem_u32(&bar_full[i]));
-  }
+  float m_run = -INFINITY, l_run = 0.f;
+  float o_acc[NT][4];
+#pragma unroll
+  for (int j = 0; j < NT; ++j) o_acc[j][0] = o_acc[j][1] = o_acc[j][2] = o_acc[j][3] = 0.f;
+  const int row = lane >> 2;  // query head of this thread's accumulator rows 0..7
 
-  const int dsl = (lane % LPK) * 8;
-  const int kr = lane / LPK;
-  float qf[G][8];
+  if (warp == kDecConsumers) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // membership words were generic writes
+      bool ok = true;
+      for (int i = 0; i < nst && ok; ++i) {
+        const int slot = i % kDecStages;
+        if (i >= kDecStages &&
+            !(ok = mbar_wait(smem_u32(&bar_empty[slot]), ((i / kDecStages) - 1) & 1, abort_v, p.err)))
+          break;
+        const int key0 = min(stage_key0(i), p.T_k);  // past T_k: zero fill, masked below
+        const uint32_t st = sbase + slot * Cfg::kStageBytes;
+        mbar_arrive_expect_tx(smem_u32(&bar_full[slot]), 2u * chk * D * 2);
 #pragma unroll
-  for (int j = 0; j < G; ++j) {
-    const uint4 u = *reinterpret_cast<const uint4*>(p.q + (int64_t)b * p.q_sb + (int64_t)(h0 + j) * p.q_sh + dsl);
-    bf16x8_to_f32(u, qf[j]);
+        for (int r = 0; r < R; ++r) {
+          tma_load_4d(st + r * kDecChunk * 128, &p.tm_k, smem_u32(&bar_full[slot]), r * 64, key0, kvh, b);
+          tma_load_4d(st + Cfg::kHalfBytes + r * kDecChunk * 128, &p.tm_v, smem_u32(&bar_full[slot]), r * 64,
+                      key0, kvh, b);
+        }
+      }
+      int zero = 0;  // drain (bounded) copies still in flight
+      for (int i = max(0, nst - kDecStages); i < nst; ++i)
+        mbar_wait(smem_u32(&bar_full[i % kDecStages]), (i / kDecStages) & 1, &zero, nullptr);
+    }
+  } else {
+    // ------------------------------------------------------------ consumers
+    // Q of the group as the A operand: rows 0..G-1 = heads, rows G..15 zero.
+    uint32_t qa[D / 16][2];
+    {
+      const __nv_bfloat16* qrow = p.q + (int64_t)b * p.q_sb + (int64_t)(h0 + row) * p.q_sh;
 #pragma unroll
-    for (int e = 0; e < 8; ++e) qf[j][e] *= p.scale_log2;
-  }
-  float m[G], l[G], o[G][8];
-#pragma unroll
-  for (int j = 0; j < G; ++j) {
-    m[j] = -INFINITY;
-    l[j] = 0.f;
-#pragma unroll
-    for (int e = 0; e < 8; ++e) o[j][e] = 0.f;
-  }
-  volatile int* abort_v = &abort_flag;
-  bool ok = true;
-  for (int i = 0; i < nst; ++i) {
-    const int slot = i % kDecStages;
-    ok = mbar_wait(smem_u32(&bar_full[slot]), (i / kDecStages) & 1, abort_v, p.err);
-    if (!__all_sync(0xffffffffu, ok)) break;
-    const int rows = stage_rows(i);
-    const uint32_t hm = s_hm[e_begin + i / nsub];
-    const uint8_t* kst = dsmem + (sK(slot) - smem_u32(dsmem));
-    const uint8_t* vst = dsmem + (sV(slot) - smem_u32(dsmem));
-    float x[IT][G];
-#pragma unroll
-    for (int it = 0; it < IT; ++it) {
-      const int r = warp * KPWARP + it * KPW + kr;
-      float kf[8];
-      bf16x8_to_f32(*reinterpret_cast<const uint4*>(kst + r * D * 2 + dsl * 2), kf);
-      const bool valid = r < rows;
-#pragma unroll
-      for (int j = 0; j < G; ++j) {
-        float d = 0.f;
-#pragma unroll
-        for (int e = 0; e < 8; ++e) d = fmaf(qf[j][e], kf[e], d);
-#pragma unroll
-        for (int off = LPK / 2; off >= 1; off >>= 1) d += __shfl_xor_sync(0xffffffffu, d, off);
-        x[it][j] = (valid && ((hm >> j) & 1u)) ? d : -INFINITY;
+      for (int kk = 0; kk < D / 16; ++kk) {
+        const int d = kk * 16 + 2 * (lane & 3);
+        qa[kk][0] = row < G ? *reinterpret_cast<const uint32_t*>(qrow + d) : 0u;
+        qa[kk][1] = row < G ? *reinterpret_cast<const uint32_t*>(qrow + d + 8) : 0u;
       }
     }
+    const int k_lo = warp * 16;  // this warp's 16 keys of each stage
+    for (int i = 0; i < nst; ++i) {
+      const int slot = i % kDecStages;
+      bool ok = mbar_wait(smem_u32(&bar_full[slot]), (i / kDecStages) & 1, abort_v, p.err);
+      if (!__all_sync(0xffffffffu, ok)) break;
+      const int key0 = stage_key0(i);
+      const int rows = max(0, min(chk, p.T_k - key0));
+      const uint32_t hm = s_hm[e_begin + i / nsub];
+      if (k_lo < rows) {
+        const uint32_t sk = sbase + slot * Cfg::kStageBytes;
+        const uint32_t sv = sk + Cfg::kHalfBytes;
+        // S = Q K^T for this warp's two 8-key n-tiles.
+        float s0[4] = {0.f, 0.f, 0.f, 0.f}, s1[4] = {0.f, 0.f, 0.f, 0.f};
+        const int kr = k_lo + (lane & 7) + ((lane >> 4) << 3);
 #pragma unroll
-    for (int j = 0; j < G; ++j) {
-      float mb = m[j];
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const int reg = kk >> 2;
+          const int ch = ((kk & 3) << 1) + ((lane >> 3) & 1);
+          uint32_t b0, b1, b2, b3;
+          ldsm_x4(sw128(sk + reg * kDecChunk * 128, kr, ch), b0, b1, b2, b3);
+          mma_bf16(s0, qa[kk][0], 0u, qa[kk][1], 0u, b0, b1);
+          mma_bf16(s1, qa[kk][0], 0u, qa[kk][1], 0u, b2, b3);
+        }
+        // mask + online softmax (rows = heads; keys 2*(lane&3)+{0,1} of each tile)
+        const bool head_ok = row < G && ((hm >> row) & 1u);
+        const int c0 = k_lo + 2 * (lane & 3);
+        float x[4];
+        x[0] = (head_ok && c0 < rows) ? s0[0] * p.scale_log2 : -INFINITY;
+        x[1] = (head_ok && c0 + 1 < rows) ? s0[1] * p.scale_log2 : -INFINITY;
+        x[2] = (head_ok && c0 + 8 < rows) ? s1[0] * p.scale_log2 : -INFINITY;
+        x[3] = (head_ok && c0 + 9 < rows) ? s1[1] * p.scale_log2 : -INFINITY;
+        float mb = fmaxf(fmaxf(x[0], x[1]), fmaxf(x[2], x[3]));
+        mb = fmaxf(mb, __shfl_xor_sync(0xffffffffu, mb, 1));
+        mb = fmaxf(mb, __shfl_xor_sync(0xffffffffu, mb, 2));
+        const float m_new = fmaxf(m_run, mb);
+        const float mu = m_new == -INFINITY ? 0.f : m_new;
+        const float alpha = ex2(m_run - mu);
+        float pr[4];
 #pragma unroll
-      for (int it = 0; it < IT; ++it) mb = fmaxf(mb, x[it][j]);
-      const float mu = mb == -INFINITY ? 0.f : mb;
-      const float alpha = ex2(m[j] - mu);
-      l[j] *= alpha;
+        for (int e = 0; e < 4; ++e) pr[e] = ex2(x[e] - mu);
+        l_run = l_run * alpha + (pr[0] + pr[1]) + (pr[2] + pr[3]);
+        m_run = m_new;
+        const uint32_t pa0 = pack_bf16(pr[0], pr[1]), pa2 = pack_bf16(pr[2], pr[3]);
+        // O = alpha * O + P V over this warp's 16 keys.
+        const int vr = k_lo + (lane & 7) + (((lane >> 3) & 1) << 3);
 #pragma unroll
-      for (int e = 0; e < 8; ++e) o[j][e] *= alpha;
-      m[j] = mb;
-    }
+        for (int j = 0; j < NT; j += 2) {
+          const int dch = j + (lane >> 4);  // 16-byte chunk index over D
+          uint32_t v0, v1, v2, v3;
+          ldsm_x4_t(sw128(sv + (dch >> 3) * kDecChunk * 128, vr, dch & 7), v0, v1, v2, v3);
 #pragma unroll
-    for (int it = 0; it < IT; ++it) {
-      const int r = warp * KPWARP + it * KPW + kr;
-      float vf[8];
-      bf16x8_to_f32(*reinterpret_cast<const uint4*>(vst + r * D * 2 + dsl * 2), vf);
-      if (r >= rows) {  // rows past T_k were not copied this time: never multiply them
-#pragma unroll
-        for (int e = 0; e < 8; ++e) vf[e] = 0.f;
+          for (int e = 0; e < 4; ++e) {
+            o_acc[j][e] *= alpha;
+            o_acc[j + 1][e] *= alpha;
+          }
+          mma_bf16(o_acc[j], pa0, 0u, pa2, 0u, v0, v1);
+          mma_bf16(o_acc[j + 1], pa0, 0u, pa2, 0u, v2, v3);
+        }
       }
-#pragma unroll
-      for (int j = 0; j < G; ++j) {
-        const float mu = m[j] == -INFINITY ? 0.f : m[j];
-        const float pj = ex2(x[it][j] - mu);
-        l[j] += pj;
-#pragma unroll
-        for (int e = 0; e < 8; ++e) o[j][e] = fmaf(pj, vf[e], o[j][e]);
-      }
-    }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(smem_u32(&bar_empty[slot]));
-    if (tid == 0 && i + kDecStages < nst) {
-      // refill this slot once every warp has consumed it
-      ok = mbar_wait(smem_u32(&bar_empty[slot]), (i / kDecStages) & 1, abort_v, p.err);
-      if (ok)
-        issue_stage<D>(p, b, kvh, stage_key0(i + kDecStages), stage_rows(i + kDecStages), sK(slot), sV(slot),
-                       smem_u32(&bar_full[slot]));
-    }
-  }
-  // Drain (bounded) copies still in flight before the ring is reused or the CTA exits.
-  if (tid == 0) {
-    int zero = 0;
-    for (int i = max(0, nst - kDecStages); i < nst; ++i)
-      mbar_wait(smem_u32(&bar_full[i % kDecStages]), (i / kDecStages) & 1, &zero, nullptr);
-  }
-  __syncthreads();  // ring idle: reuse it for the per-warp partials
-  // Merge the KPW key rows of a warp (lanes with equal d-slice).
-#pragma unroll
-  for (int off = LPK; off < 32; off <<= 1) {
-#pragma unroll
-    for (int j = 0; j < G; ++j) {
-      const float mo = __shfl_xor_sync(0xffffffffu, m[j], off);
-      const float lo = __shfl_xor_sync(0xffffffffu, l[j], off);
-      const float mn = fmaxf(m[j], mo);
-      const float mu = mn == -INFINITY ? 0.f : mn;
-      const float a = ex2(m[j] - mu), c = ex2(mo - mu);
-      l[j] = l[j] * a + lo * c;
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        const float oo = __shfl_xor_sync(0xffffffffu, o[j][e], off);
-        o[j][e] = o[j][e] * a + oo * c;
-      }
-      m[j] = mn;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&bar_empty[slot]));
     }
   }
-  if (kr == 0) {
+  DEC_TRACE(2);
+  __syncthreads();  // ring idle (producer drained): reuse it for the per-warp partials
+  if (warp < kDecConsumers) {
+    float l_row = l_run;
+    l_row += __shfl_xor_sync(0xffffffffu, l_row, 1);
+    l_row += __shfl_xor_sync(0xffffffffu, l_row, 2);
+    if ((lane & 3) == 0) {
+      s_m[warp][row] = m_run;
+      s_l[warp][row] = l_row;
+    }
 #pragma unroll
-    for (int j = 0; j < G; ++j) {
-#pragma unroll
-      for (int e = 0; e < 8; ++e) s_o[warp][j][dsl + e] = o[j][e];
-      if (lane == 0) {
-        s_m[warp][j] = m[j];
-        s_l[warp][j] = l[j];
-      }
+    for (int j = 0; j < NT; ++j) {
+      s_o[warp][row][j * 8 + 2 * (lane & 3)] = o_acc[j][0];
+      s_o[warp][row][j * 8 + 2 * (lane & 3) + 1] = o_acc[j][1];
     }
   }
   __syncthreads();
-  // Merge the warps: one thread per (head, d).
+  // Merge the consumer warps: one thread per (head, d).
   for (int idx = tid; idx < G * D; idx += kDecThreads) {
     const int j = idx / D, d = idx % D;
     float mx = -INFINITY;
 #pragma unroll
-    for (int w = 0; w < kDecWarps; ++w) mx = fmaxf(mx, s_m[w][j]);
+    for (int w = 0; w < kDecConsumers; ++w) mx = fmaxf(mx, s_m[w][j]);
     const float mu = mx == -INFINITY ? 0.f : mx;
     float lsum = 0.f, acc = 0.f;
 #pragma unroll
-    for (int w = 0; w < kDecWarps; ++w) {
+    for (int w = 0; w < kDecConsumers; ++w) {
       const float c = ex2(s_m[w][j] - mu);
       lsum += s_l[w][j] * c;
       acc += s_o[w][j][d] * c;
     }
-    const int64_t rowi = ((int64_t)b * p.Hq + h0 + j) * p.n_split + split;
-    p.part_o[rowi * D + d] = acc;
-    if (d == 0) {
-      p.part_ml[rowi * 2] = mx;
-      p.part_ml[rowi * 2 + 1] = lsum;
+    if (p.n_split == 1) {
+      p.out[(int64_t)b * p.o_sb + (int64_t)(h0 + j) * p.o_sh + d] = __float2bfloat16_rn(lsum > 0.f ? acc / lsum : 0.f);
+    } else {
+      const int64_t rowi = ((int64_t)b * p.Hq + h0 + j) * p.n_split + split;
+      p.part_o[rowi * D + d] = acc;
+      if (d == 0) {
+        p.part_ml[rowi * 2] = mx;
+        p.part_ml[rowi * 2 + 1] = lsum;
+      }
     }
   }
+  DEC_TRACE(3);
 }
 
 template <int D>
@@ -373,10 +387,12 @@ static int launch_decode(const DecodeParams& prm, const sa_attn_args* a, cudaStr
                                      DecodeCfg<D>::kSmemBytes));
   decode_split_kernel<D, G><<<grid, kDecThreads, DecodeCfg<D>::kSmemBytes, stream>>>(prm);
   SA_CHECK_CUDA(cudaGetLastError());
-  decode_combine_kernel<D><<<prm.B * prm.Hq, D, 0, stream>>>(
-      prm.part_o, prm.part_ml, reinterpret_cast<__nv_bfloat16*>(a->out), a->o_strides[0],
-      a->o_strides[1], prm.Hq, prm.n_split);
-  SA_CHECK_CUDA(cudaGetLastError());
+  if (prm.n_split > 1) {
+    decode_combine_kernel<D><<<prm.B * prm.Hq, D, 0, stream>>>(
+        prm.part_o, prm.part_ml, reinterpret_cast<__nv_bfloat16*>(a->out), a->o_strides[0],
+        a->o_strides[1], prm.Hq, prm.n_split);
+    SA_CHECK_CUDA(cudaGetLastError());
+  }
   return SA_OK;
 }
 
@@ -398,17 +414,15 @@ int sa_decode_prepare(const sa_attn_args* a, int32_t n_split, float* partial_o, 
   if (n_split < 1 || n_split > 64) return sa_fail(SA_ERR_INVALID, "n_split %d not in [1, 64]", n_split);
   if (!partial_o || !partial_ml) return sa_fail(SA_ERR_INVALID, "NULL scratch pointer");
   memset(prm, 0, sizeof(*prm));
+  prm->chk = a->block_size < kDecChunk ? a->block_size : kDecChunk;
+  if ((rc = sa_make_map(&prm->tm_k, a->k, a->B, a->Hkv, a->T_k, a->D, a->k_strides, prm->chk, "k"))) return rc;
+  if ((rc = sa_make_map(&prm->tm_v, a->v, a->B, a->Hkv, a->T_k, a->D, a->v_strides, prm->chk, "v"))) return rc;
   prm->q = reinterpret_cast<const __nv_bfloat16*>(a->q);
-  prm->k = reinterpret_cast<const __nv_bfloat16*>(a->k);
-  prm->v = reinterpret_cast<const __nv_bfloat16*>(a->v);
   prm->q_sb = a->q_strides[0];
   prm->q_sh = a->q_strides[1];
-  prm->k_sb = a->k_strides[0];
-  prm->k_sh = a->k_strides[1];
-  prm->k_st = a->k_strides[2];
-  prm->v_sb = a->v_strides[0];
-  prm->v_sh = a->v_strides[1];
-  prm->v_st = a->v_strides[2];
+  prm->out = reinterpret_cast<__nv_bfloat16*>(a->out);
+  prm->o_sb = a->o_strides[0];
+  prm->o_sh = a->o_strides[1];
   prm->pairs = a->pairs;
   prm->offsets = a->offsets;
   prm->pairs_stride = a->pairs_stride;
@@ -490,3 +504,11 @@ extern "C" int sa_decode_fwd_noalloc(const sa_attn_args* a, int32_t n_split, sa_
   if (rc) return rc;
   return sa_decode_launch(prm, a, reinterpret_cast<cudaStream_t>(stream));
 }
+
+#ifdef SA_PHASE_TRACE
+extern "C" SA_API int sa_debug_dec_trace_read(unsigned long long* host, int n) {
+  SA_CHECK_CUDA(cudaDeviceSynchronize());
+  SA_CHECK_CUDA(cudaMemcpyFromSymbol(host, sa::g_dec_trace, sizeof(unsigned long long) * (n < 16384 ? n : 16384)));
+  return SA_OK;
+}
+#endif

@@ -570,41 +570,6 @@ __global__ void __launch_bounds__(kThreads, CTAS) prefill_kernel(const __grid_co
 // ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
-typedef CUresult (*PFN_encodeTiled_t)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
-                                      const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
-                                      const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
-                                      CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-static PFN_encodeTiled_t get_encode_fn() {
-  static PFN_encodeTiled_t fn = nullptr;
-  if (!fn) {
-    void* ptr = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
-            cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_encodeTiled_t>(ptr);
-  }
-  return fn;
-}
-
-// 4-D bf16 map over [B, H, T, D] (innermost first: D, T, H, B), box (64, rows, 1, 1).
-static int make_map(CUtensorMap* m, const void* base, int B, int H, int T, int D,
-                    const int64_t strides[3], int box_rows, const char* name) {
-  PFN_encodeTiled_t enc = get_encode_fn();
-  if (!enc) return sa_fail(SA_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
-  cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)T, (cuuint64_t)H, (cuuint64_t)B};
-  cuuint64_t gstr[3] = {(cuuint64_t)strides[2] * 2, (cuuint64_t)strides[1] * 2,
-                        (cuuint64_t)strides[0] * 2};
-  cuuint32_t box[4] = {64, (cuuint32_t)box_rows, 1, 1};
-  cuuint32_t estr[4] = {1, 1, 1, 1};
-  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, gstr, box,
-                   estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return sa_fail(SA_ERR_INVALID, "tensor map for %s rejected (CUresult %d)", name, (int)r);
-  return SA_OK;
-}
-
 template <int D, int N, int CTAS>
 static int launch_prefill(const PrefillParams& prm, int64_t ntiles, int sms, cudaStream_t stream) {
   using Cfg = PrefillCfg<D, N, CTAS>;
@@ -668,9 +633,9 @@ extern "C" int sa_prefill_fwd(const sa_attn_args* a, sa_stream_t stream_) {
   const int N = bs >= chunk ? chunk : bs;
   PrefillParams prm;
   memset(&prm, 0, sizeof(prm));
-  if ((rc = make_map(&prm.tm_q, a->q, a->B, a->Hq, a->T_q, a->D, a->q_strides, kTileM, "q"))) return rc;
-  if ((rc = make_map(&prm.tm_k, a->k, a->B, a->Hkv, a->T_k, a->D, a->k_strides, N, "k"))) return rc;
-  if ((rc = make_map(&prm.tm_v, a->v, a->B, a->Hkv, a->T_k, a->D, a->v_strides, N, "v"))) return rc;
+  if ((rc = sa_make_map(&prm.tm_q, a->q, a->B, a->Hq, a->T_q, a->D, a->q_strides, kTileM, "q"))) return rc;
+  if ((rc = sa_make_map(&prm.tm_k, a->k, a->B, a->Hkv, a->T_k, a->D, a->k_strides, N, "k"))) return rc;
+  if ((rc = sa_make_map(&prm.tm_v, a->v, a->B, a->Hkv, a->T_k, a->D, a->v_strides, N, "v"))) return rc;
   prm.out = reinterpret_cast<__nv_bfloat16*>(a->out);
   prm.o_sb = a->o_strides[0];
   prm.o_sh = a->o_strides[1];

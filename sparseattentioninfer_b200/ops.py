@@ -198,8 +198,10 @@ def prefill_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, block_pairs: 
 
 
 def default_n_split(q: torch.Tensor, k: torch.Tensor) -> int:
+    # One CTA per (b, kv head) already fills the GPU once there are ~#SMs of
+    # them (measured: more splits only repeat the per-CTA union build).
     B, Hkv = k.shape[0], k.shape[1]
-    target = 4 * _num_sms(q.device)
+    target = _num_sms(q.device)
     return int(min(64, max(1, math.ceil(target / max(1, B * Hkv)))))
 
 
