@@ -39,6 +39,7 @@ __device__ unsigned long long g_sa_trace[16 * 512];
   do {                                                                                 \
     if (blockIdx.x == 0 && (step) < 512) g_sa_trace[(step) * 16 + (slot)] = clock64(); \
   } while (0)
+__device__ unsigned long long g_sa_cta_trace[1024 * 2];
 #else
 #define SA_TRACE(step, slot) \
   do {                       \
@@ -57,9 +58,11 @@ struct PrefillParams {
   int32_t B, Hq, Hkv, T_q, T_k, bs, nqb, nqt, group;
   float scale_log2;
   int32_t* err;
+  uint32_t* sched;  // {next tile, CTAs finished} of this launch's scheduler slot
 };
 
-constexpr int kThreads = 192;  // warp 0 producer, warp 1 MMA issuer, warps 2..5 softmax
+constexpr int kThreads = 192;
+constexpr int kTileRing = 4;  // warp 0 producer, warp 1 MMA issuer, warps 2..5 softmax
 constexpr int kTileM = 128;
 constexpr int kMaxSeg = 8;  // 128 / 16
 // Chunk metadata ring. The producer runs at most kKStages chunks ahead of the
@@ -195,6 +198,8 @@ __global__ void __launch_bounds__(kThreads, CTAS) prefill_kernel(const __grid_co
   __shared__ int meta_key0[kMetaRing];
   __shared__ uint32_t meta_mask[kMetaRing];
   __shared__ int meta_last[kMetaRing];
+  __shared__ __align__(8) uint64_t bar_tile[kTileRing];
+  __shared__ int tile_ring[kTileRing];
   __shared__ uint32_t tmem_base_sh;
   __shared__ int abort_flag;
 
@@ -208,6 +213,13 @@ __global__ void __launch_bounds__(kThreads, CTAS) prefill_kernel(const __grid_co
   const int lane = threadIdx.x & 31;
   const int ntiles = p.nqt * p.B * p.Hq;
   const bool misaligned = (sQ & 1023u) != 0;
+#ifdef SA_PHASE_TRACE
+  if (threadIdx.x == 0 && blockIdx.x < 1024) {
+    unsigned long long t_;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));
+    g_sa_cta_trace[blockIdx.x * 2] = t_;
+  }
+#endif
 
   if (threadIdx.x == 0) {
     if (misaligned) record_error(p.err, SA_DEV_ERR_INDEX);
@@ -224,6 +236,7 @@ __global__ void __launch_bounds__(kThreads, CTAS) prefill_kernel(const __grid_co
       mbar_init(smem_u32(&bar_v_empty[i]), 1);
     }
     for (int i = 0; i < kMetaRing; ++i) mbar_init(smem_u32(&bar_meta[i]), 1);
+    for (int i = 0; i < kTileRing; ++i) mbar_init(smem_u32(&bar_tile[i]), 1);
     for (int i = 0; i < 2; ++i) mbar_init(smem_u32(&bar_p_full[i]), 128);
     abort_flag = 0;
     fence_mbar_init();
@@ -253,7 +266,15 @@ __global__ void __launch_bounds__(kThreads, CTAS) prefill_kernel(const __grid_co
       uint32_t g = 0;
       int it = 0, q_issued = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x, ++it) {
+      // Dynamic schedule: tiles are taken in order from the launch's counter
+      // (head-major, heaviest tile of a head first) and published to the MMA and
+      // softmax warps through the tile ring; -1 ends the CTA's work.
+      for (;; ++it) {
+        int t = (int)atomicAdd(&p.sched[0], 1u);
+        if (t >= ntiles) t = -1;
+        tile_ring[it % kTileRing] = t;
+        mbar_arrive(smem_u32(&bar_tile[it % kTileRing]));
+        if (t < 0) break;
         const TileCoord c = tile_coord<N>(p, t);
         const int kvh = c.h / p.group;
         if (it > 0 && !(ok = mbar_wait(smem_u32(&bar_q_empty), (it - 1) & 1, abort_v, p.err))) break;
@@ -348,7 +369,9 @@ __global__ void __launch_bounds__(kThreads, CTAS) prefill_kernel(const __grid_co
         mma_commit(smem_u32(&bar_k_empty[ks]));
         SA_TRACE(gg, 5);
       };
-      for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x, ++it) {
+      for (;; ++it) {
+        if (!(ok = mbar_wait(smem_u32(&bar_tile[it % kTileRing]), (it / kTileRing) & 1, abort_v, p.err))) break;
+        if (tile_ring[it % kTileRing] < 0) break;
         if (!(ok = mbar_wait(smem_u32(&bar_q_full), it & 1, abort_v, p.err))) break;
         tc_fence_after();
         if (!(ok = mbar_wait(smem_u32(&bar_k_full[g % NSK]), (g / NSK) & 1, abort_v, p.err))) break;
@@ -401,7 +424,11 @@ __global__ void __launch_bounds__(kThreads, CTAS) prefill_kernel(const __grid_co
     uint32_t g = 0;
     int it = 0;
     bool ok = true;
-    for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x, ++it) {
+    for (;; ++it) {
+      ok = mbar_wait(smem_u32(&bar_tile[it % kTileRing]), (it / kTileRing) & 1, abort_v, p.err);
+      if (!__all_sync(FULL, ok)) break;
+      const int t = tile_ring[it % kTileRing];
+      if (t < 0) break;
       const TileCoord c = tile_coord<N>(p, t);
       const int q_local = c.q0 + row;
       const int q_abs = q_local + (p.T_k - p.T_q);
@@ -565,11 +592,48 @@ __global__ void __launch_bounds__(kThreads, CTAS) prefill_kernel(const __grid_co
   __syncthreads();
   tc_fence_after();
   if (warp == 1) tmem_dealloc(tmem, Cfg::kTmemCols);
+  if (threadIdx.x == 0) {
+    // The last CTA to finish rearms the scheduler slot for a later launch.
+    __threadfence();
+    if (atomicAdd(&p.sched[1], 1u) == gridDim.x - 1) {
+      p.sched[0] = 0;
+      p.sched[1] = 0;
+      __threadfence();
+    }
+  }
+#ifdef SA_PHASE_TRACE
+  if (threadIdx.x == 0 && blockIdx.x < 1024) {
+    unsigned long long t_;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));
+    g_sa_cta_trace[blockIdx.x * 2 + 1] = t_;
+  }
+#endif
 }
 
 // ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
+// Scheduler slots: {next tile, CTAs finished} per launch, zero between launches
+// (the last CTA of a launch resets its slot). Launches take slots round robin,
+// so up to kSchedSlots prefill launches may be in flight at once on a device.
+constexpr int kSchedSlots = 64;
+__device__ uint32_t g_sa_sched[kSchedSlots][2];
+
+static int sched_slot(uint32_t** out) {
+  static uint32_t* base[64] = {nullptr};
+  static unsigned seq[64] = {0};
+  int dev = 0;
+  SA_CHECK_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return sa_fail(SA_ERR_UNSUPPORTED, "device index %d out of range", dev);
+  if (!base[dev]) {
+    void* p = nullptr;
+    SA_CHECK_CUDA(cudaGetSymbolAddress(&p, g_sa_sched));
+    base[dev] = static_cast<uint32_t*>(p);
+  }
+  *out = base[dev] + 2 * (__sync_fetch_and_add(&seq[dev], 1u) % kSchedSlots);
+  return SA_OK;
+}
+
 template <int D, int N, int CTAS>
 static int launch_prefill(const PrefillParams& prm, int64_t ntiles, int sms, cudaStream_t stream) {
   using Cfg = PrefillCfg<D, N, CTAS>;
@@ -654,6 +718,7 @@ extern "C" int sa_prefill_fwd(const sa_attn_args* a, sa_stream_t stream_) {
   prm.group = a->Hq / a->Hkv;
   prm.scale_log2 = a->scale * 1.4426950408889634f;
   prm.err = sa_device_error_ptr();
+  if ((rc = sched_slot(&prm.sched))) return rc;
   const int64_t ntiles = (int64_t)prm.nqt * a->B * a->Hq;
   if (ntiles > 0x7fffffff) return sa_fail(SA_ERR_INVALID, "too many tiles");
   int sms = a->num_sms > 0 ? a->num_sms : sa_num_sms();
@@ -678,6 +743,11 @@ extern "C" int sa_prefill_fwd(const sa_attn_args* a, sa_stream_t stream_) {
 extern "C" SA_API int sa_debug_trace_clear() {
   static unsigned long long zeros[16 * 512];
   SA_CHECK_CUDA(cudaMemcpyToSymbol(sa::g_sa_trace, zeros, sizeof(zeros)));
+  return SA_OK;
+}
+extern "C" SA_API int sa_debug_cta_trace_read(unsigned long long* host, int n) {
+  SA_CHECK_CUDA(cudaDeviceSynchronize());
+  SA_CHECK_CUDA(cudaMemcpyFromSymbol(host, sa::g_sa_cta_trace, sizeof(unsigned long long) * (n < 2048 ? n : 2048)));
   return SA_OK;
 }
 extern "C" SA_API int sa_debug_trace_read(unsigned long long* host, int n) {
