@@ -61,7 +61,6 @@ struct PrefillParams {
   uint32_t* sched;  // {next tile, CTAs finished} of this launch's scheduler slot
 };
 
-constexpr int kThreads = 192;
 constexpr int kTileRing = 4;  // warp 0 producer, warp 1 MMA issuer, warps 2..5 softmax
 constexpr int kTileM = 128;
 constexpr int kMaxSeg = 8;  // 128 / 16
@@ -70,27 +69,34 @@ constexpr int kMaxSeg = 8;  // 128 / 16
 // never rewritten before the softmax has read it.
 constexpr int kMetaRing = 16;
 
-template <int D, int N, int CTAS>
+template <int D, int N, int CTAS, int LANES>
 struct PrefillCfg {
   static constexpr int kRegions = D / 64;               // 64-column (128 B) slabs
   static constexpr int kQBytes = kTileM * D * 2;
   static constexpr int kKVBytes = N * D * 2;            // one K (or V) chunk
-  // TMEM: O in columns [0, D), two S/P buffers of kSStride columns after it.
+  // TMEM per lane: O in columns [0, D), then kSBufs S/P buffers of kSStride
+  // columns. With two lanes each lane has one S buffer: the other lane's MMAs
+  // fill the tensor core while this lane's softmax runs.
+  static constexpr int kSBufs = LANES == 1 ? 2 : 1;
   static constexpr int kSStride = N < 32 ? 32 : N;
-  static constexpr int kTmemNeed = D + 2 * kSStride;
-  static constexpr int kTmemCols = kTmemNeed <= 32 ? 32 : kTmemNeed <= 64 ? 64 : kTmemNeed <= 128 ? 128
-                                   : kTmemNeed <= 256 ? 256 : 512;
+  static constexpr int kLaneNeed = D + kSBufs * kSStride;
+  static constexpr int kLaneCols = kLaneNeed <= 32 ? 32 : kLaneNeed <= 64 ? 64 : kLaneNeed <= 128 ? 128
+                                   : kLaneNeed <= 256 ? 256 : 512;
+  static constexpr int kTmemCols = kLaneCols * LANES;
   static_assert(kTmemCols * CTAS <= 512, "TMEM over-subscribed");
   // 228 KB of shared memory per SM, of which 1 KB per resident CTA is reserved
-  // by the hardware and 1 KB holds this kernel's static shared data.
-  static constexpr int kSmemBudget = (233472 / CTAS) - 2048;
-  static constexpr int kBufs = (kSmemBudget - kQBytes) / kKVBytes;  // K + V chunk buffers
+  // by the hardware; static shared data is kept under LANES KB.
+  static constexpr int kSmemBudget = (233472 / CTAS) - 1024 - 1024 * LANES;
+  static constexpr int kLaneBudget = kSmemBudget / LANES;
+  static constexpr int kBufs = (kLaneBudget - kQBytes) / kKVBytes;  // K + V chunk buffers per lane
   static constexpr int kKHalf = kBufs / 2 + (kBufs & 1);
   static constexpr int kKStages = kKHalf > 4 ? 4 : kKHalf;
   static constexpr int kVStages = (kBufs - kKStages) > 4 ? 4 : (kBufs - kKStages);
-  static constexpr int kSmemBytes = kQBytes + (kKStages + kVStages) * kKVBytes;
-  static_assert(kVStages >= 2, "not enough shared memory for the K/V rings");
+  static constexpr int kLaneBytes = kQBytes + (kKStages + kVStages) * kKVBytes;
+  static constexpr int kSmemBytes = kLaneBytes * LANES;
+  static_assert(kVStages >= 1 && kKStages >= 1, "not enough shared memory for the K/V rings");
   static_assert(kKStages + 3 < kMetaRing, "meta ring too short");
+  static constexpr int kThreads = LANES * 192;  // per lane: producer, MMA issuer, 4 softmax warps
 };
 
 // Chunk stream of one tile: sorted union of up to kMaxSeg CSR rows, each key
@@ -182,37 +188,44 @@ __device__ __forceinline__ TileCoord tile_coord(const PrefillParams& p, int t) {
   return c;
 }
 
-template <int D, int N, int CTAS>
-__global__ void __launch_bounds__(kThreads, CTAS) prefill_kernel(const __grid_constant__ PrefillParams p) {
-  using Cfg = PrefillCfg<D, N, CTAS>;
-  constexpr uint32_t SB = D;                  // first S/P buffer column
+// One lane = one tile at a time through its own producer, K/V rings, MMA
+// issuer and softmax warpgroup. Warps of lane L: 6L producer, 6L+1 MMA issuer,
+// 6L+2 .. 6L+5 softmax (their warp index mod 4 covers the four TMEM lane
+// quadrants). With LANES = 2 the two lanes' MMAs interleave on the tensor core.
+template <int D, int N, int CTAS, int LANES>
+__global__ void __launch_bounds__(LANES * 192, CTAS) prefill_kernel(const __grid_constant__ PrefillParams p) {
+  using Cfg = PrefillCfg<D, N, CTAS, LANES>;
+  constexpr uint32_t SB = D;                  // first S/P buffer column (within a lane)
   constexpr uint32_t SS = Cfg::kSStride;      // S/P buffer stride (columns)
+  constexpr int NSB = Cfg::kSBufs;
   constexpr int NSK = Cfg::kKStages;
   constexpr int NSV = Cfg::kVStages;
   constexpr int R = Cfg::kRegions;
 
-  __shared__ __align__(8) uint64_t bar_q_full, bar_q_empty, bar_o_empty, bar_drain;
-  __shared__ __align__(8) uint64_t bar_k_full[NSK], bar_k_empty[NSK], bar_v_full[NSV], bar_v_empty[NSV];
-  __shared__ __align__(8) uint64_t bar_p_full[2];
-  __shared__ __align__(8) uint64_t bar_meta[kMetaRing];
-  __shared__ int meta_key0[kMetaRing];
-  __shared__ uint32_t meta_mask[kMetaRing];
-  __shared__ int meta_last[kMetaRing];
-  __shared__ __align__(8) uint64_t bar_tile[kTileRing];
-  __shared__ int tile_ring[kTileRing];
+  __shared__ __align__(8) uint64_t bar_q_full[LANES], bar_q_empty[LANES], bar_o_empty[LANES], bar_drain[LANES];
+  __shared__ __align__(8) uint64_t bar_k_full[LANES][NSK], bar_k_empty[LANES][NSK];
+  __shared__ __align__(8) uint64_t bar_v_full[LANES][NSV], bar_v_empty[LANES][NSV];
+  __shared__ __align__(8) uint64_t bar_p_full[LANES][2];
+  __shared__ __align__(8) uint64_t bar_meta[LANES][kMetaRing];
+  __shared__ __align__(8) uint64_t bar_tile[LANES][kTileRing];
+  __shared__ int meta_key0[LANES][kMetaRing];
+  __shared__ uint32_t meta_mask[LANES][kMetaRing];
+  __shared__ int meta_last[LANES][kMetaRing];
+  __shared__ int tile_ring[LANES][kTileRing];
   __shared__ uint32_t tmem_base_sh;
   __shared__ int abort_flag;
 
-  // Dynamic shared memory: Q | K ring | V ring, 1024-byte aligned for SWIZZLE_128B.
+  // Dynamic shared memory per lane: Q | K ring | V ring, 1024-byte aligned for SWIZZLE_128B.
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  const uint32_t sQ = smem_u32(smem_raw);
-  const uint32_t sK = sQ + Cfg::kQBytes;
-  const uint32_t sV = sK + NSK * Cfg::kKVBytes;
-
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  const int L = warp / 6;        // tile lane of this warp
+  const int role = warp % 6;     // 0 producer, 1 MMA issuer, 2..5 softmax
+  const uint32_t sQ = smem_u32(smem_raw) + L * Cfg::kLaneBytes;
+  const uint32_t sK = sQ + Cfg::kQBytes;
+  const uint32_t sV = sK + NSK * Cfg::kKVBytes;
   const int ntiles = p.nqt * p.B * p.Hq;
-  const bool misaligned = (sQ & 1023u) != 0;
+  const bool misaligned = (smem_u32(smem_raw) & 1023u) != 0;
 #ifdef SA_PHASE_TRACE
   if (threadIdx.x == 0 && blockIdx.x < 1024) {
     unsigned long long t_;
@@ -223,21 +236,23 @@ __global__ void __launch_bounds__(kThreads, CTAS) prefill_kernel(const __grid_co
 
   if (threadIdx.x == 0) {
     if (misaligned) record_error(p.err, SA_DEV_ERR_INDEX);
-    mbar_init(smem_u32(&bar_q_full), 1);
-    mbar_init(smem_u32(&bar_q_empty), 1);
-    mbar_init(smem_u32(&bar_o_empty), 128);
-    mbar_init(smem_u32(&bar_drain), 1);
-    for (int i = 0; i < NSK; ++i) {
-      mbar_init(smem_u32(&bar_k_full[i]), 1);
-      mbar_init(smem_u32(&bar_k_empty[i]), 1);
+    for (int l = 0; l < LANES; ++l) {
+      mbar_init(smem_u32(&bar_q_full[l]), 1);
+      mbar_init(smem_u32(&bar_q_empty[l]), 1);
+      mbar_init(smem_u32(&bar_o_empty[l]), 128);
+      mbar_init(smem_u32(&bar_drain[l]), 1);
+      for (int i = 0; i < NSK; ++i) {
+        mbar_init(smem_u32(&bar_k_full[l][i]), 1);
+        mbar_init(smem_u32(&bar_k_empty[l][i]), 1);
+      }
+      for (int i = 0; i < NSV; ++i) {
+        mbar_init(smem_u32(&bar_v_full[l][i]), 1);
+        mbar_init(smem_u32(&bar_v_empty[l][i]), 1);
+      }
+      for (int i = 0; i < kMetaRing; ++i) mbar_init(smem_u32(&bar_meta[l][i]), 1);
+      for (int i = 0; i < kTileRing; ++i) mbar_init(smem_u32(&bar_tile[l][i]), 1);
+      for (int i = 0; i < 2; ++i) mbar_init(smem_u32(&bar_p_full[l][i]), 128);
     }
-    for (int i = 0; i < NSV; ++i) {
-      mbar_init(smem_u32(&bar_v_full[i]), 1);
-      mbar_init(smem_u32(&bar_v_empty[i]), 1);
-    }
-    for (int i = 0; i < kMetaRing; ++i) mbar_init(smem_u32(&bar_meta[i]), 1);
-    for (int i = 0; i < kTileRing; ++i) mbar_init(smem_u32(&bar_tile[i]), 1);
-    for (int i = 0; i < 2; ++i) mbar_init(smem_u32(&bar_p_full[i]), 128);
     abort_flag = 0;
     fence_mbar_init();
   }
@@ -253,35 +268,35 @@ __global__ void __launch_bounds__(kThreads, CTAS) prefill_kernel(const __grid_co
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem = tmem_base_sh;
+  const uint32_t tmem = tmem_base_sh + L * Cfg::kLaneCols;
   volatile int* abort_v = &abort_flag;
 
   if (misaligned) {
     // dynamic shared memory not 1024-byte aligned (recorded above): do nothing
-  } else if (warp == 0) {
+  } else if (role == 0) {
     // ------------------------------------------------------------------ producer
-    // One thread. Per chunk: metadata (+ its barrier), K into the K ring once
-    // its slot's S=QK^T retired, V into the V ring once its slot's PV retired.
+    // One thread. Dynamic schedule: tiles come in order from the launch's
+    // counter (head-major, heaviest tile of a head first) and are published to
+    // this lane's MMA and softmax warps through the tile ring; -1 ends the lane.
+    // Per chunk: metadata (+ its barrier), K into the K ring once its slot's
+    // S=QK^T retired, V into the V ring once its slot's PV retired.
     if (lane == 0) {
       uint32_t g = 0;
       int it = 0, q_issued = 0;
       bool ok = true;
-      // Dynamic schedule: tiles are taken in order from the launch's counter
-      // (head-major, heaviest tile of a head first) and published to the MMA and
-      // softmax warps through the tile ring; -1 ends the CTA's work.
       for (;; ++it) {
         int t = (int)atomicAdd(&p.sched[0], 1u);
         if (t >= ntiles) t = -1;
-        tile_ring[it % kTileRing] = t;
-        mbar_arrive(smem_u32(&bar_tile[it % kTileRing]));
+        tile_ring[L][it % kTileRing] = t;
+        mbar_arrive(smem_u32(&bar_tile[L][it % kTileRing]));
         if (t < 0) break;
         const TileCoord c = tile_coord<N>(p, t);
         const int kvh = c.h / p.group;
-        if (it > 0 && !(ok = mbar_wait(smem_u32(&bar_q_empty), (it - 1) & 1, abort_v, p.err))) break;
-        mbar_arrive_expect_tx(smem_u32(&bar_q_full), Cfg::kQBytes);
+        if (it > 0 && !(ok = mbar_wait(smem_u32(&bar_q_empty[L]), (it - 1) & 1, abort_v, p.err))) break;
+        mbar_arrive_expect_tx(smem_u32(&bar_q_full[L]), Cfg::kQBytes);
 #pragma unroll
         for (int r = 0; r < R; ++r)
-          tma_load_4d(sQ + r * kTileM * 128, &p.tm_q, smem_u32(&bar_q_full), r * 64, c.q0, c.h, c.b);
+          tma_load_4d(sQ + r * kTileM * 128, &p.tm_q, smem_u32(&bar_q_full[L]), r * 64, c.q0, c.h, c.b);
         ++q_issued;
         ChunkStream cs;
         cs.init(p, c.h, c.qb0, c.nseg, c.nsub);
@@ -300,48 +315,49 @@ __global__ void __launch_bounds__(kThreads, CTAS) prefill_kernel(const __grid_co
           const int kcoord = min(key0, p.T_k);  // fully out-of-range chunks read zeros
           const int ks = g % NSK, vs = g % NSV, ms = g % kMetaRing;
           if (g >= (uint32_t)NSK &&
-              !(ok = mbar_wait(smem_u32(&bar_k_empty[ks]), ((g / NSK) - 1) & 1, abort_v, p.err)))
+              !(ok = mbar_wait(smem_u32(&bar_k_empty[L][ks]), ((g / NSK) - 1) & 1, abort_v, p.err)))
             break;
-          meta_key0[ms] = key0;
-          meta_mask[ms] = cur_mask;
-          meta_last[ms] = more ? 0 : 1;
-          mbar_arrive(smem_u32(&bar_meta[ms]));
-          mbar_arrive_expect_tx(smem_u32(&bar_k_full[ks]), Cfg::kKVBytes);
+          meta_key0[L][ms] = key0;
+          meta_mask[L][ms] = cur_mask;
+          meta_last[L][ms] = more ? 0 : 1;
+          mbar_arrive(smem_u32(&bar_meta[L][ms]));
+          mbar_arrive_expect_tx(smem_u32(&bar_k_full[L][ks]), Cfg::kKVBytes);
 #pragma unroll
           for (int r = 0; r < R; ++r)
-            tma_load_4d(sK + ks * Cfg::kKVBytes + r * N * 128, &p.tm_k, smem_u32(&bar_k_full[ks]), r * 64, kcoord,
-                        kvh, c.b);
-          SA_TRACE(g, 13);
+            tma_load_4d(sK + ks * Cfg::kKVBytes + r * N * 128, &p.tm_k, smem_u32(&bar_k_full[L][ks]), r * 64,
+                        kcoord, kvh, c.b);
+          if (L == 0) SA_TRACE(g, 13);
           if (g >= (uint32_t)NSV &&
-              !(ok = mbar_wait(smem_u32(&bar_v_empty[vs]), ((g / NSV) - 1) & 1, abort_v, p.err)))
+              !(ok = mbar_wait(smem_u32(&bar_v_empty[L][vs]), ((g / NSV) - 1) & 1, abort_v, p.err)))
             break;
-          mbar_arrive_expect_tx(smem_u32(&bar_v_full[vs]), Cfg::kKVBytes);
+          mbar_arrive_expect_tx(smem_u32(&bar_v_full[L][vs]), Cfg::kKVBytes);
 #pragma unroll
           for (int r = 0; r < R; ++r)
-            tma_load_4d(sV + vs * Cfg::kKVBytes + r * N * 128, &p.tm_v, smem_u32(&bar_v_full[vs]), r * 64, kcoord,
-                        kvh, c.b);
-          SA_TRACE(g, 14);
+            tma_load_4d(sV + vs * Cfg::kKVBytes + r * N * 128, &p.tm_v, smem_u32(&bar_v_full[L][vs]), r * 64,
+                        kcoord, kvh, c.b);
+          if (L == 0) SA_TRACE(g, 14);
           ++g;
           if (!more) break;
           cur_kb = cs.kb;
           cur_mask = cs.mask;
           cur_sub = cs.sub;
         }
+        if (!ok) break;
       }
       // Drain: wait (bounded, ignoring the abort flag) for copies still in flight.
       int zero = 0;
       volatile int* never = &zero;
       for (uint32_t i = 0; i < (g < (uint32_t)NSK ? g : (uint32_t)NSK); ++i) {
         const uint32_t gi = g - 1 - i;
-        mbar_wait(smem_u32(&bar_k_full[gi % NSK]), (gi / NSK) & 1, never, nullptr);
+        mbar_wait(smem_u32(&bar_k_full[L][gi % NSK]), (gi / NSK) & 1, never, nullptr);
       }
       for (uint32_t i = 0; i < (g < (uint32_t)NSV ? g : (uint32_t)NSV); ++i) {
         const uint32_t gi = g - 1 - i;
-        mbar_wait(smem_u32(&bar_v_full[gi % NSV]), (gi / NSV) & 1, never, nullptr);
+        mbar_wait(smem_u32(&bar_v_full[L][gi % NSV]), (gi / NSV) & 1, never, nullptr);
       }
-      if (q_issued > 0) mbar_wait(smem_u32(&bar_q_full), (q_issued - 1) & 1, never, nullptr);
+      if (q_issued > 0) mbar_wait(smem_u32(&bar_q_full[L]), (q_issued - 1) & 1, never, nullptr);
     }
-  } else if (warp == 1) {
+  } else if (role == 1) {
     // ------------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc_s = idesc_bf16_f32(128, N, false);
@@ -358,7 +374,7 @@ __global__ void __launch_bounds__(kThreads, CTAS) prefill_kernel(const __grid_co
       // and tells the softmax that S is in TMEM.
       auto issue_s = [&](uint32_t gg) {
         const int ks = gg % NSK;
-        const uint32_t d = tmem + SB + (gg & 1) * SS;
+        const uint32_t d = tmem + SB + (gg % NSB) * SS;
         const uint64_t kst = k_desc + (uint64_t)((ks * Cfg::kKVBytes) >> 4);
 #pragma unroll
         for (int k = 0; k < D / 16; ++k) {
@@ -366,57 +382,66 @@ __global__ void __launch_bounds__(kThreads, CTAS) prefill_kernel(const __grid_co
           mma_ss(d, q_desc + ((r * kTileM * 128 + kk * 32) >> 4), kst + ((r * N * 128 + kk * 32) >> 4), idesc_s,
                  k > 0 ? 1u : 0u);
         }
-        mma_commit(smem_u32(&bar_k_empty[ks]));
-        SA_TRACE(gg, 5);
+        mma_commit(smem_u32(&bar_k_empty[L][ks]));
+        if (L == 0) SA_TRACE(gg, 5);
+      };
+      // Wait for K of chunk gg, then issue its S (and release Q after the tile's last S).
+      auto next_s = [&](uint32_t gg, int& last) -> bool {
+        if (!mbar_wait(smem_u32(&bar_k_full[L][gg % NSK]), (gg / NSK) & 1, abort_v, p.err)) return false;
+        tc_fence_after();
+        last = meta_last[L][gg % kMetaRing];
+        issue_s(gg);
+        if (last) mma_commit(smem_u32(&bar_q_empty[L]));
+        return true;
       };
       for (;; ++it) {
-        if (!(ok = mbar_wait(smem_u32(&bar_tile[it % kTileRing]), (it / kTileRing) & 1, abort_v, p.err))) break;
-        if (tile_ring[it % kTileRing] < 0) break;
-        if (!(ok = mbar_wait(smem_u32(&bar_q_full), it & 1, abort_v, p.err))) break;
+        if (!(ok = mbar_wait(smem_u32(&bar_tile[L][it % kTileRing]), (it / kTileRing) & 1, abort_v, p.err))) break;
+        if (tile_ring[L][it % kTileRing] < 0) break;
+        if (!(ok = mbar_wait(smem_u32(&bar_q_full[L]), it & 1, abort_v, p.err))) break;
         tc_fence_after();
-        if (!(ok = mbar_wait(smem_u32(&bar_k_full[g % NSK]), (g / NSK) & 1, abort_v, p.err))) break;
-        tc_fence_after();
-        int last = meta_last[g % kMetaRing];
-        issue_s(g);
-        if (last) mma_commit(smem_u32(&bar_q_empty));
+        int last = 0;
         const uint32_t g0 = g;
+        if (!(ok = next_s(g0, last))) break;
         while (true) {
           const bool cur_last = last;
-          const uint32_t gn = g + 1;
-          if (!cur_last) {
-            if (!(ok = mbar_wait(smem_u32(&bar_k_full[gn % NSK]), (gn / NSK) & 1, abort_v, p.err))) break;
-            tc_fence_after();
-            last = meta_last[gn % kMetaRing];
-            issue_s(gn);
-            if (last) mma_commit(smem_u32(&bar_q_empty));
-          }
-          if (!(ok = mbar_wait(smem_u32(&bar_p_full[g & 1]), (g >> 1) & 1, abort_v, p.err))) break;
-          SA_TRACE(g, 6);
-          if (g == g0 && it > 0 && !(ok = mbar_wait(smem_u32(&bar_o_empty), (it - 1) & 1, abort_v, p.err))) break;
+          // Two S buffers: S of the next chunk goes in before this chunk's PV.
+          if (NSB == 2 && !cur_last && !(ok = next_s(g + 1, last))) break;
+          if (!(ok = mbar_wait(smem_u32(&bar_p_full[L][g & 1]), (g >> 1) & 1, abort_v, p.err))) break;
+          if (L == 0) SA_TRACE(g, 6);
+          if (g == g0 && it > 0 &&
+              !(ok = mbar_wait(smem_u32(&bar_o_empty[L]), (it - 1) & 1, abort_v, p.err)))
+            break;
           const int vs = g % NSV;
-          if (!(ok = mbar_wait(smem_u32(&bar_v_full[vs]), (g / NSV) & 1, abort_v, p.err))) break;
+          if (!(ok = mbar_wait(smem_u32(&bar_v_full[L][vs]), (g / NSV) & 1, abort_v, p.err))) break;
           tc_fence_after();
-          const uint32_t pbuf = tmem + SB + (g & 1) * SS;
+          const uint32_t pbuf = tmem + SB + (g % NSB) * SS;
           const uint64_t vst = v_desc + (uint64_t)((vs * Cfg::kKVBytes) >> 4);
           const uint32_t acc0 = g != g0 ? 1u : 0u;
 #pragma unroll
-          for (int k = 0; k < N / 16; ++k) mma_ts(tmem, pbuf + k * 8, vst + ((k * 2048) >> 4), idesc_pv, k > 0 ? 1u : acc0);
-          mma_commit(smem_u32(&bar_v_empty[vs]));  // PV_g retired: V slot free, O holds chunk g
-          SA_TRACE(g, 7);
-          g = gn;
+          for (int k = 0; k < N / 16; ++k)
+            mma_ts(tmem, pbuf + k * 8, vst + ((k * 2048) >> 4), idesc_pv, k > 0 ? 1u : acc0);
+          mma_commit(smem_u32(&bar_v_empty[L][vs]));  // PV_g retired: V slot free, O holds chunk g
+          if (L == 0) SA_TRACE(g, 7);
+          // One S buffer: the next S reuses it once this PV (reading P) is issued.
+          if (NSB == 1 && !cur_last && !(ok = next_s(g + 1, last))) break;
+          ++g;
           if (cur_last) break;
         }
+        if (!ok) break;
       }
       // Drain this thread's outstanding MMAs before TMEM is released.
-      mma_commit(smem_u32(&bar_drain));
+      mma_commit(smem_u32(&bar_drain[L]));
       int zero = 0;
-      mbar_wait(smem_u32(&bar_drain), 0, &zero, nullptr);
+      mbar_wait(smem_u32(&bar_drain[L]), 0, &zero, nullptr);
     }
   } else {
     // ------------------------------------------------------------------ softmax
     // "S_j in TMEM" is completion of K slot j%NSK and "PV_j retired" that of V
     // slot j%NSV: neither can advance a second phase before this warpgroup has
     // consumed chunk j, so the parity waits are exact.
+    // S is read in two passes of 64-column halves (row max, then exponentials
+    // and P) so that no thread holds a whole 128-column row in registers.
+    constexpr int HALF = N >= 64 ? 64 : N;  // columns per pass step
     const int wr = warp & 3;  // TMEM lane quadrant this warp may access
     const int row = wr * 32 + lane;
     const uint32_t lane_base = (uint32_t)(wr * 32) << 16;
@@ -425,9 +450,9 @@ __global__ void __launch_bounds__(kThreads, CTAS) prefill_kernel(const __grid_co
     int it = 0;
     bool ok = true;
     for (;; ++it) {
-      ok = mbar_wait(smem_u32(&bar_tile[it % kTileRing]), (it / kTileRing) & 1, abort_v, p.err);
+      ok = mbar_wait(smem_u32(&bar_tile[L][it % kTileRing]), (it / kTileRing) & 1, abort_v, p.err);
       if (!__all_sync(FULL, ok)) break;
-      const int t = tile_ring[it % kTileRing];
+      const int t = tile_ring[L][it % kTileRing];
       if (t < 0) break;
       const TileCoord c = tile_coord<N>(p, t);
       const int q_local = c.q0 + row;
@@ -439,54 +464,61 @@ __global__ void __launch_bounds__(kThreads, CTAS) prefill_kernel(const __grid_co
       bool first = true;
       while (true) {
         const int ms = g % kMetaRing;
-        ok = mbar_wait(smem_u32(&bar_meta[ms]), (g / kMetaRing) & 1, abort_v, p.err);
+        ok = mbar_wait(smem_u32(&bar_meta[L][ms]), (g / kMetaRing) & 1, abort_v, p.err);
         if (!__all_sync(FULL, ok)) { ok = false; break; }
-        const int key0 = meta_key0[ms];
-        const uint32_t mask = meta_mask[ms];
-        const int last = meta_last[ms];
-        if (threadIdx.x == 64) SA_TRACE(g, 0);
-        ok = mbar_wait(smem_u32(&bar_k_empty[g % NSK]), (g / NSK) & 1, abort_v, p.err);
-        if (threadIdx.x == 64) SA_TRACE(g, 1);
+        const int key0 = meta_key0[L][ms];
+        const uint32_t mask = meta_mask[L][ms];
+        const int last = meta_last[L][ms];
+        if (L == 0 && threadIdx.x == 64) SA_TRACE(g, 0);
+        ok = mbar_wait(smem_u32(&bar_k_empty[L][g % NSK]), (g / NSK) & 1, abort_v, p.err);
+        if (L == 0 && threadIdx.x == 64) SA_TRACE(g, 1);
         if (!__all_sync(FULL, ok)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t sbuf = tmem + lane_base + SB + (g & 1) * SS;
-        float s[N];
-        if constexpr (N >= 32) {
-          uint32_t r32[N / 32][32];
-#pragma unroll
-          for (int cc = 0; cc < N / 32; ++cc) tmem_ld32(sbuf + cc * 32, r32[cc]);
-          tmem_wait_ld();
-#pragma unroll
-          for (int cc = 0; cc < N / 32; ++cc) {
-            reg_fence32(r32[cc]);
-#pragma unroll
-            for (int i = 0; i < 32; ++i) s[cc * 32 + i] = __uint_as_float(r32[cc][i]);
-          }
-        } else {
-          uint32_t r16[16];
-          tmem_ld16(sbuf, r16);
-          tmem_wait_ld();
-          reg_fence16(r16);
-#pragma unroll
-          for (int i = 0; i < 16; ++i) s[i] = __uint_as_float(r16[i]);
-        }
-        if (threadIdx.x == 64) SA_TRACE(g, 2);
+        const uint32_t sbuf = tmem + lane_base + SB + (g % NSB) * SS;
         const bool mine = row_ok && ((mask >> seg) & 1u);
         const bool full_ok = mine && (key0 + N - 1 <= q_abs) && (key0 + N <= p.T_k);
-        if (!full_ok) {
-          const int lim = min(q_abs, p.T_k - 1) - key0;  // valid columns: i <= lim
+        const int lim = min(q_abs, p.T_k - 1) - key0;  // valid columns: i <= lim
+        // Load columns [h0, h0 + HALF) of S, masked when needed.
+        auto load_half = [&](int h0, float (&s)[HALF]) {
+          if constexpr (HALF >= 32) {
+            uint32_t r32[HALF / 32][32];
 #pragma unroll
-          for (int i = 0; i < N; ++i) s[i] = (mine && i <= lim) ? s[i] : -INFINITY;
+            for (int cc = 0; cc < HALF / 32; ++cc) tmem_ld32(sbuf + h0 + cc * 32, r32[cc]);
+            tmem_wait_ld();
+#pragma unroll
+            for (int cc = 0; cc < HALF / 32; ++cc) {
+              reg_fence32(r32[cc]);
+#pragma unroll
+              for (int i = 0; i < 32; ++i) s[cc * 32 + i] = __uint_as_float(r32[cc][i]);
+            }
+          } else {
+            uint32_t r16[16];
+            tmem_ld16(sbuf + h0, r16);
+            tmem_wait_ld();
+            reg_fence16(r16);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) s[i] = __uint_as_float(r16[i]);
+          }
+          if (!full_ok) {
+#pragma unroll
+            for (int i = 0; i < HALF; ++i) s[i] = (mine && h0 + i <= lim) ? s[i] : -INFINITY;
+          }
+        };
+        // Pass 1: raw-score row max (three-input max chains; the positive
+        // scale is folded into the exponent below).
+        float mraw = -INFINITY;
+#pragma unroll 1
+        for (int h0 = 0; h0 < N; h0 += HALF) {
+          float s[HALF];
+          load_half(h0, s);
+          float mx8[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) mx8[i] = s[i];
+#pragma unroll
+          for (int i = 8; i < HALF; i += 2) mx8[(i >> 1) & 7] = max3(mx8[(i >> 1) & 7], s[i], s[i + 1]);
+          mraw = max3(mraw, fmaxf(max3(mx8[0], mx8[1], mx8[2]), mx8[3]), max3(mx8[4], mx8[5], fmaxf(mx8[6], mx8[7])));
         }
-        // Raw-score row max with 8 independent chains; the positive scale is
-        // folded into the exponent below.
-        float mx8[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) mx8[i] = s[i];
-#pragma unroll
-        for (int i = 8; i < N; ++i) mx8[i & 7] = fmaxf(mx8[i & 7], s[i]);
-        const float mraw = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
-                                 fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+        if (L == 0 && threadIdx.x == 64) SA_TRACE(g, 2);
         const float m_new = fmaxf(m_ref, mraw * p.scale_log2);
         if (first) {
           m_ref = m_new;
@@ -494,7 +526,7 @@ __global__ void __launch_bounds__(kThreads, CTAS) prefill_kernel(const __grid_co
           const bool need = m_new > m_ref + 8.0f;
           if (__any_sync(FULL, need)) {
             // O still holds the previous chunk's PV: wait for it, then rescale.
-            ok = mbar_wait(smem_u32(&bar_v_empty[(g - 1) % NSV]), ((g - 1) / NSV) & 1, abort_v, p.err);
+            ok = mbar_wait(smem_u32(&bar_v_empty[L][(g - 1) % NSV]), ((g - 1) / NSV) & 1, abort_v, p.err);
             if (!__all_sync(FULL, ok)) { ok = false; break; }
             tc_fence_after();
             const float alpha = need ? ex2(m_ref - m_new) : 1.0f;
@@ -516,52 +548,53 @@ __global__ void __launch_bounds__(kThreads, CTAS) prefill_kernel(const __grid_co
           }
         }
         const float m_use = (m_ref == -INFINITY) ? 0.f : m_ref;
-        const float nm = -m_use;
-        uint32_t pk[N / 2];
-        float rs8[8];
+        const uint64_t sc2 = f2pack(p.scale_log2, p.scale_log2), nm2 = f2pack(-m_use, -m_use);
+        uint64_t rs4[4];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) rs8[i] = 0.f;
+        for (int i = 0; i < 4; ++i) rs4[i] = 0ull;
+        // Pass 2: exponentials, row sum, and P (bf16 pairs) written over the
+        // first N/2 columns of this S buffer, HALF/2 columns per step (those
+        // columns were read by this or the previous step).
+#pragma unroll 1
+        for (int h0 = 0; h0 < N; h0 += HALF) {
+          float s[HALF];
+          load_half(h0, s);
+          uint32_t pk[HALF / 2];
 #pragma unroll
-        for (int i = 0; i < N / 2; ++i) {
-          const float p0 = ex2(fmaf(s[2 * i], p.scale_log2, nm));
-          const float p1 = ex2(fmaf(s[2 * i + 1], p.scale_log2, nm));
-          rs8[(2 * i) & 7] += p0;
-          rs8[(2 * i + 1) & 7] += p1;
-          pk[i] = pack_bf16(p0, p1);
-        }
-        l += ((rs8[0] + rs8[1]) + (rs8[2] + rs8[3])) + ((rs8[4] + rs8[5]) + (rs8[6] + rs8[7]));
-        if (threadIdx.x == 64) SA_TRACE(g, 3);
-        // P (bf16 pairs) overwrites the first N/2 columns of this S buffer.
-        if constexpr (N / 2 >= 32) {
-#pragma unroll
-          for (int cc = 0; cc < N / 64; ++cc) {
-            uint32_t w32[32];
-#pragma unroll
-            for (int i = 0; i < 32; ++i) w32[i] = pk[cc * 32 + i];
-            tmem_st32(sbuf + cc * 32, w32);
+          for (int i = 0; i < HALF / 2; ++i) {
+            float x0, x1;
+            f2unpack(fma2(f2pack(s[2 * i], s[2 * i + 1]), sc2, nm2), x0, x1);
+            const float p0 = ex2(x0), p1 = ex2(x1);
+            rs4[i & 3] = add2(rs4[i & 3], f2pack(p0, p1));
+            pk[i] = pack_bf16(p0, p1);
           }
-        } else if constexpr (N / 2 == 16) {
-          uint32_t w16[16];
-#pragma unroll
-          for (int i = 0; i < 16; ++i) w16[i] = pk[i];
-          tmem_st16(sbuf, w16);
-        } else {
-          uint32_t w8[8];
-#pragma unroll
-          for (int i = 0; i < 8; ++i) w8[i] = pk[i];
-          tmem_st8(sbuf, w8);
+          const uint32_t pdst = sbuf + h0 / 2;
+          if constexpr (HALF / 2 >= 32) {
+            tmem_st32(pdst, pk);
+          } else if constexpr (HALF / 2 == 16) {
+            tmem_st16(pdst, pk);
+          } else {
+            tmem_st8(pdst, pk);
+          }
         }
+        {
+          float a0, a1, b0, b1;
+          f2unpack(add2(rs4[0], rs4[1]), a0, a1);
+          f2unpack(add2(rs4[2], rs4[3]), b0, b1);
+          l += (a0 + a1) + (b0 + b1);
+        }
+        if (L == 0 && threadIdx.x == 64) SA_TRACE(g, 3);
         tmem_wait_st();
         tc_fence_before();
-        mbar_arrive(smem_u32(&bar_p_full[g & 1]));
-        if (threadIdx.x == 64) SA_TRACE(g, 4);
+        mbar_arrive(smem_u32(&bar_p_full[L][g & 1]));
+        if (L == 0 && threadIdx.x == 64) SA_TRACE(g, 4);
         ++g;
         first = false;
         if (last) break;
       }
       if (!ok) break;
       // ---------------------------------------------------------------- epilogue
-      ok = mbar_wait(smem_u32(&bar_v_empty[(g - 1) % NSV]), ((g - 1) / NSV) & 1, abort_v, p.err);
+      ok = mbar_wait(smem_u32(&bar_v_empty[L][(g - 1) % NSV]), ((g - 1) / NSV) & 1, abort_v, p.err);
       if (!__all_sync(FULL, ok)) { ok = false; break; }
       tc_fence_after();
       const float inv = l > 0.f ? 1.0f / l : 0.f;
@@ -571,7 +604,7 @@ __global__ void __launch_bounds__(kThreads, CTAS) prefill_kernel(const __grid_co
       for (int cc = 0; cc < D / 32; ++cc) tmem_ld32(tmem + lane_base + cc * 32, o32[cc]);
       tmem_wait_ld();
       tc_fence_before();
-      mbar_arrive(smem_u32(&bar_o_empty));  // O is in registers: the next tile may overwrite TMEM
+      mbar_arrive(smem_u32(&bar_o_empty[L]));  // O is in registers: the next tile may overwrite TMEM
 #pragma unroll
       for (int cc = 0; cc < D / 32; ++cc) {
         reg_fence32(o32[cc]);
@@ -591,7 +624,7 @@ __global__ void __launch_bounds__(kThreads, CTAS) prefill_kernel(const __grid_co
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 1) tmem_dealloc(tmem, Cfg::kTmemCols);
+  if (warp == 1) tmem_dealloc(tmem_base_sh, Cfg::kTmemCols);
   if (threadIdx.x == 0) {
     // The last CTA to finish rearms the scheduler slot for a later launch.
     __threadfence();
@@ -634,16 +667,15 @@ static int sched_slot(uint32_t** out) {
   return SA_OK;
 }
 
-template <int D, int N, int CTAS>
+template <int D, int N, int CTAS, int LANES>
 static int launch_prefill(const PrefillParams& prm, int64_t ntiles, int sms, cudaStream_t stream) {
-  using Cfg = PrefillCfg<D, N, CTAS>;
-  SA_CHECK_CUDA(cudaFuncSetAttribute(prefill_kernel<D, N, CTAS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     Cfg::kSmemBytes));
-  SA_CHECK_CUDA(cudaFuncSetAttribute(prefill_kernel<D, N, CTAS>, cudaFuncAttributePreferredSharedMemoryCarveout,
-                                     100));
+  using Cfg = PrefillCfg<D, N, CTAS, LANES>;
+  auto kern = prefill_kernel<D, N, CTAS, LANES>;
+  SA_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes));
+  SA_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
   const int64_t slots = (int64_t)sms * CTAS;
   const int grid = (int)(ntiles < slots ? ntiles : slots);
-  prefill_kernel<D, N, CTAS><<<grid, kThreads, Cfg::kSmemBytes, stream>>>(prm);
+  kern<<<grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(prm);
   SA_CHECK_CUDA(cudaGetLastError());
   return SA_OK;
 }
@@ -727,14 +759,14 @@ extern "C" int sa_prefill_fwd(const sa_attn_args* a, sa_stream_t stream_) {
   // warpgroups interleave on the tensor core), or 128 keys with one CTA per SM
   // (SA_PREFILL_CHUNK=128).
   switch (a->D * 10000 + N) {
-    case 1280128: return launch_prefill<128, 128, 1>(prm, ntiles, sms, stream);
-    case 1280064: return launch_prefill<128, 64, 2>(prm, ntiles, sms, stream);
-    case 1280032: return launch_prefill<128, 32, 2>(prm, ntiles, sms, stream);
-    case 1280016: return launch_prefill<128, 16, 2>(prm, ntiles, sms, stream);
-    case 640128: return launch_prefill<64, 128, 1>(prm, ntiles, sms, stream);
-    case 640064: return launch_prefill<64, 64, 2>(prm, ntiles, sms, stream);
-    case 640032: return launch_prefill<64, 32, 2>(prm, ntiles, sms, stream);
-    case 640016: return launch_prefill<64, 16, 2>(prm, ntiles, sms, stream);
+    case 1280128: return launch_prefill<128, 128, 1, 2>(prm, ntiles, sms, stream);
+    case 1280064: return launch_prefill<128, 64, 2, 1>(prm, ntiles, sms, stream);
+    case 1280032: return launch_prefill<128, 32, 2, 1>(prm, ntiles, sms, stream);
+    case 1280016: return launch_prefill<128, 16, 2, 1>(prm, ntiles, sms, stream);
+    case 640128: return launch_prefill<64, 128, 1, 2>(prm, ntiles, sms, stream);
+    case 640064: return launch_prefill<64, 64, 2, 1>(prm, ntiles, sms, stream);
+    case 640032: return launch_prefill<64, 32, 2, 1>(prm, ntiles, sms, stream);
+    case 640016: return launch_prefill<64, 16, 2, 1>(prm, ntiles, sms, stream);
   }
   return sa_fail(SA_ERR_UNSUPPORTED, "no kernel for D=%d chunk=%d", a->D, N);
 }
