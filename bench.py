@@ -230,6 +230,98 @@ def time_decode(device) -> dict:
 
 
 
+
+def time_gqa_layer(device, rank: int, world: int) -> dict:
+    """Config 3: GQA layer with Qwen3-4B shapes, B=2, Hq=32, Hkv=8, D=128,
+    S=16384 bf16; q and k get per-head RMSNorm (unit weight) and RoPE (theta 1e6);
+    per-KV-group BigBird layouts (block 64) drawn from seed 2 (workloads.config3_group_layouts).
+    With N ranks, rank r owns KV groups [r*8/N, (r+1)*8/N) and their query heads."""
+    from sparseattentioninfer_b200 import ops, workloads as wl
+    B3, Hq, Hkv, S3, D3 = 2, 32, 8, 16384, 128
+    layouts = wl.config3_group_layouts()
+    gpr = max(1, Hkv // world)  # KV groups per rank
+    g0 = (rank * gpr) % Hkv
+    hq = gpr * (Hq // Hkv)
+    q, k, v = wl.seeded_qkv(30 + rank, B3, hq, gpr, S3, S3, D3, device=device, dtype=torch.bfloat16)
+    q, k = wl.rope(wl.rms_norm(q)), wl.rope(wl.rms_norm(k))
+    # the reference indexes random blocks by the global query-head index: compile the
+    # full layer's CSR and keep this rank's rows, so every shard matches the whole layer
+    pairs, offs = ops.compile_bigbird(layouts, Hq, S3, S3, 64, device=device)
+    h_lo = g0 * (Hq // Hkv)
+    pairs, offs = pairs[h_lo:h_lo + hq].contiguous(), offs[h_lo:h_lo + hq].contiguous()
+    nnz = int(offs[:, -1].long().sum().item())
+    flops = 4 * 64 * 64 * D3 * nnz * B3
+    out = torch.empty_like(q)
+    for _ in range(3):
+        ops.prefill_fwd(q, k, v, pairs, offs, 64, out=out)
+    ts = []
+    for _ in range(20):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        ops.prefill_fwd(q, k, v, pairs, offs, 64, out=out)
+        e1.record()
+        e1.synchronize()
+        ts.append(e0.elapsed_time(e1) / 1e3)
+    t = statistics.median(ts)
+    return {"workload": "gqa_qwen3_4b_b2_h32kv8_s16384_d128_bigbird64_groups_seed2", "kv_groups_per_rank": gpr,
+            "layouts": [list(x) for x in layouts], "retained_blocks": nnz * B3, "ms": t * 1e3,
+            "tflops": flops / t / 1e12, "flops": flops}
+
+
+
+def time_tp_model(device, rank: int, world: int, *, prompt=65536, steps=512, batch=8, chunk=4096,
+                  seed=0) -> dict:
+    """Config 5: random-init Qwen3-8B architecture (hidden 4096, 36 layers, 32/8
+    heads, head_dim 128, SwiGLU 12288, vocab 151936, weights N(0, 0.02)) in bf16,
+    tensor-parallel over the KV groups (sparseattentioninfer_b200.tp; NCCL
+    all-reduce after o_proj and down_proj), BigBird (128, 2, 4, 3) in every layer;
+    batch 8, prefill of `prompt` uniform-random token ids, then `steps` greedy
+    decode steps. TTFT = prefill through the first token's logits and argmax;
+    times are CUDA events, max over ranks."""
+    from sparseattentioninfer_b200 import tp
+    torch.cuda.empty_cache()
+    w = tp.Qwen3TPWeights(tp.QWEN3_8B, rank, world, seed=seed, device=device)
+    runner = tp.Qwen3TPRunner(w, batch, prompt + steps + 8, (128, 2, 4, 3))
+    tok = torch.randint(0, tp.QWEN3_8B.vocab, (batch, prompt), generator=torch.Generator().manual_seed(5))
+    tok = tok.to(device)
+
+    def sync():
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize()
+
+    # warm: a short prefill + decode builds cuBLAS/NCCL state and the decode CSR path
+    runner.prefill(tok[:, :2 * chunk], chunk=chunk)
+    t = tok[:, :1]
+    for _ in range(4):
+        t = runner.step(t)
+    sync()
+    e = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+    e[0].record()
+    logits = runner.prefill(tok, chunk=chunk)
+    t = logits.argmax(-1, keepdim=True)
+    e[1].record()
+    sync()
+    e[2].record()
+    for _ in range(steps):
+        t = runner.step(t)
+    e[3].record()
+    sync()
+    ttft, dec = e[0].elapsed_time(e[1]) / 1e3, e[2].elapsed_time(e[3]) / 1e3
+    if world > 1:
+        tt = torch.tensor([ttft, dec], device=device)
+        torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.MAX)
+        ttft, dec = (float(x) for x in tt.tolist())
+    res = {"workload": f"qwen3_8b_arch_tp{world}_b{batch}_prompt{prompt}_decode{steps}_bigbird128_2_4_3",
+           "ttft_s": ttft, "prefill_tok_s": batch * prompt / ttft, "decode_tok_s": batch * steps / dec,
+           "decode_ms_per_step": dec / steps * 1e3, "n_gpus": world,
+           "collective": "NCCL all-reduce (bf16 sum) after o_proj and down_proj" if world > 1 else "none",
+           "weights": "random N(0,0.02), drawn per full matrix then sliced (same model at every N)",
+           "last_token": int(t[0, 0].item())}
+    del runner, w, logits
+    torch.cuda.empty_cache()
+    return res
+
 def time_qwen3_decode(device, layers=36, batch=32, ctx=32768, steps=256, chunk=1024, sparse_layers=18,
                       seed=0) -> dict:
     """Config 4: random-init Qwen3-4B architecture (hidden 2560, 36 layers, 32/8 heads,
@@ -384,6 +476,20 @@ def run_ours(args) -> None:
         barrier()
         e2e_elapsed = f0.elapsed_time(f1) / 1e3
     clocks = cs.summary()
+    gqa = time_gqa_layer(device, rank, world)
+    if world > 1:
+        gt = torch.tensor([gqa["ms"]], device=device)
+        torch.distributed.all_reduce(gt, op=torch.distributed.ReduceOp.MAX)
+        fl = torch.tensor([float(gqa["flops"])], device=device, dtype=torch.float64)
+        torch.distributed.all_reduce(fl)
+        gqa["ms_max_over_ranks"] = float(gt.item())
+        gqa["tflops_all_ranks"] = float(fl.item()) / (float(gt.item()) * 1e-3) / 1e12
+    tp_model = None
+    if args.tp_model == "on":
+        try:
+            tp_model = time_tp_model(device, rank, world, prompt=args.tp_prompt, steps=args.tp_steps)
+        except Exception as e:  # noqa: BLE001
+            tp_model = {"error": repr(e)[:300]}
 
     t_launch = statistics.median(per)
     if world > 1:
@@ -433,6 +539,9 @@ def run_ours(args) -> None:
         line["decode"]["traffic"] = traffic_from_profile("decode_qwen3_4b_layer_ncu.txt")
     except Exception as e:  # noqa: BLE001
         line["decode"] = {"error": repr(e)}
+    line["gqa_layer"] = gqa
+    if tp_model is not None:
+        line["tp_model"] = tp_model
     if args.model != "off" and world == 1:
         del q, k, v, out, md
         torch.cuda.empty_cache()
@@ -466,6 +575,10 @@ def main() -> None:
     ap.add_argument("--model-layers", type=int, default=36)
     ap.add_argument("--model-ctx", type=int, default=32768)
     ap.add_argument("--model-steps", type=int, default=256)
+    ap.add_argument("--tp-model", choices=["on", "off"], default="on",
+                    help="also time the tensor-parallel Qwen3-8B-shaped model (config 5) on all ranks")
+    ap.add_argument("--tp-prompt", type=int, default=65536)
+    ap.add_argument("--tp-steps", type=int, default=512)
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

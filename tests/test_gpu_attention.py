@@ -184,3 +184,21 @@ def test_errors_raise_not_fallback():
         ops.prefill_fwd(q, q, q, pairs, offs, 128)
     with pytest.raises(NotImplementedError):
         sa.get_backend("cuda_sm100").forward(q, q, q, sa.TopKPattern(8).build(q, q))
+
+
+def test_config3_full_size_gqa_layer_heads_vs_oracle():
+    """Config 3 at full size (B=2, Hq=32, Hkv=8, S=16384, D=128 bf16, per-KV-group
+    BigBird layouts, q/k RMSNorm + RoPE): the kernel over all heads, the oracle on
+    three query heads from different KV groups (one per GQA position)."""
+    from sparseattentioninfer_b200 import workloads as wl
+    layouts = wl.config3_group_layouts()
+    q, k, v = wl.seeded_qkv(30, 2, 32, 8, 16384, 16384, 128, device=DEV, dtype=torch.bfloat16)
+    q, k = wl.rope(wl.rms_norm(q)), wl.rope(wl.rms_norm(k))
+    pairs, offs = ops.compile_bigbird(layouts, 32, 16384, 16384, 64, device=DEV)
+    out = ops.prefill_fwd(q, k, v, pairs, offs, 64)
+    heads = [0, 13, 31]
+    ref = oracle.csr_attention(q.cpu(), k.cpu(), v.cpu(), pairs.cpu().numpy(), offs.cpu().numpy(), 64,
+                               row_chunk=2048, heads=heads)
+    for h in heads:
+        assert_close(out[:, h], ref[:, h].numpy(), f"config3 head {h}")
+    assert _capi.device_error() == 0
