@@ -281,7 +281,7 @@ def time_tp_model(device, rank: int, world: int, *, prompt=65536, steps=512, bat
     from sparseattentioninfer_b200 import tp
     torch.cuda.empty_cache()
     w = tp.Qwen3TPWeights(tp.QWEN3_8B, rank, world, seed=seed, device=device)
-    runner = tp.Qwen3TPRunner(w, batch, prompt + steps + 8, (128, 2, 4, 3))
+    runner = tp.Qwen3TPRunner(w, batch, prompt + steps + 64, (128, 2, 4, 3))
     tok = torch.randint(0, tp.QWEN3_8B.vocab, (batch, prompt), generator=torch.Generator().manual_seed(5))
     tok = tok.to(device)
 
@@ -290,37 +290,52 @@ def time_tp_model(device, rank: int, world: int, *, prompt=65536, steps=512, bat
             torch.distributed.barrier()
         torch.cuda.synchronize()
 
-    # warm: a short prefill + decode builds cuBLAS/NCCL state and the decode CSR path
+    # warm: a short prefill + eager decode builds cuBLAS/NCCL state, then the
+    # decode step is captured once as a CUDA graph (as a server does at start-up)
     runner.prefill(tok[:, :2 * chunk], chunk=chunk)
     t = tok[:, :1]
     for _ in range(4):
         t = runner.step(t)
+    runner.capture_decode()
     sync()
-    e = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+    e = [torch.cuda.Event(enable_timing=True) for _ in range(6)]
     e[0].record()
     logits = runner.prefill(tok, chunk=chunk)
     t = logits.argmax(-1, keepdim=True)
     e[1].record()
     sync()
     e[2].record()
-    for _ in range(steps):
-        t = runner.step(t)
+    g = runner.step_graph(t)
+    for _ in range(steps - 1):
+        g = runner.step_graph()
     e[3].record()
     sync()
+    last = int(g[0, 0].item())
+    # eager decode (one launch per op) on a few more steps, for the host-overhead comparison
+    eager_steps = 32
+    t = g.clone()
+    e[4].record()
+    for _ in range(eager_steps):
+        t = runner.step(t)
+    e[5].record()
+    sync()
     ttft, dec = e[0].elapsed_time(e[1]) / 1e3, e[2].elapsed_time(e[3]) / 1e3
+    dec_eager = e[4].elapsed_time(e[5]) / 1e3
     if world > 1:
-        tt = torch.tensor([ttft, dec], device=device)
+        tt = torch.tensor([ttft, dec, dec_eager], device=device)
         torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.MAX)
-        ttft, dec = (float(x) for x in tt.tolist())
+        ttft, dec, dec_eager = (float(x) for x in tt.tolist())
     res = {"workload": f"qwen3_8b_arch_tp{world}_b{batch}_prompt{prompt}_decode{steps}_bigbird128_2_4_3",
            "ttft_s": ttft, "prefill_tok_s": batch * prompt / ttft, "decode_tok_s": batch * steps / dec,
-           "decode_ms_per_step": dec / steps * 1e3, "n_gpus": world,
+           "decode_ms_per_step": dec / steps * 1e3, "decode": "CUDA graph per step (captured once)",
+           "decode_eager_tok_s": batch * eager_steps / dec_eager, "n_gpus": world,
            "collective": "NCCL all-reduce (bf16 sum) after o_proj and down_proj" if world > 1 else "none",
            "weights": "random N(0,0.02), drawn per full matrix then sliced (same model at every N)",
-           "last_token": int(t[0, 0].item())}
+           "last_token": last}
     del runner, w, logits
     torch.cuda.empty_cache()
     return res
+
 
 def time_qwen3_decode(device, layers=36, batch=32, ctx=32768, steps=256, chunk=1024, sparse_layers=18,
                       seed=0) -> dict:

@@ -185,6 +185,65 @@ SA_API int sa_decode_fwd(const sa_attn_args* args, int32_t n_split, float* parti
  * caller. Every split result is fully rewritten by each call, so nothing has to
  * start at zero. Same arguments, output and limits as sa_decode_fwd otherwise.
  * ------------------------------------------------------------------------- */
+/* ---------------------------------------------------------------------------
+ * sa_decode_fwd with the key count read from device memory: args->k / args->v
+ * span args->T_k rows (the cache capacity) and the kernel attends to keys
+ * [0, *seq_len) (clamped to [0, args->T_k]), so one launch recorded into a CUDA
+ * graph serves every step of a growing cache. The caller keeps the CSR rows
+ * valid for the live length (the decode row of block (*seq_len - 1) / bs).
+ * Rows past *seq_len are read in whole 64-key stages and masked; they must hold
+ * finite values (a zero-initialised cache does). Replaces the same decode call
+ * as sa_decode_fwd; the reference passes the length on the host.
+ * ------------------------------------------------------------------------- */
+SA_API int sa_decode_fwd_seqlen(const sa_attn_args* args, const int32_t* seq_len, int32_t n_split,
+                                float* partial_o, float* partial_ml, sa_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * Decoder-layer steps around attention (Qwen3 layer arithmetic; bf16 tensors,
+ * fp32 arithmetic, one rounding per stored value).
+ *
+ * sa_qk_norm_rope_append: from the fused projection output qkv [B, T, Hq+2*Hkv, D]
+ * (element strides qkv_sb, qkv_st; heads contiguous), writes
+ *   q_out[b, h, t]            = RoPE(RMSNorm(q) * q_weight) at position pos + t,
+ *   k_cache[b, h, pos + t]    = RoPE(RMSNorm(k) * k_weight),
+ *   v_cache[b, h, pos + t]    = v,
+ * with rotate-half RoPE from the cos/sin tables [capacity, D]. pos is *pos_dev
+ * when pos_dev is non-NULL (graph replays), else the host value. Replaces the
+ * hook's q_norm / k_norm / apply_rotary_pos_emb / cache update
+ * (modeling_sparse_qwen3.py:211-231). D in {64, 128}.
+ * ------------------------------------------------------------------------- */
+typedef struct sa_qkv_prologue_args {
+  const void* qkv;
+  int64_t qkv_sb, qkv_st;
+  const void* q_weight;   /* [D] */
+  const void* k_weight;   /* [D] */
+  const void* cos;        /* [capacity, D] */
+  const void* sin;        /* [capacity, D] */
+  void* q_out;            /* [B, Hq, T, D] */
+  int64_t q_strides[3];   /* b, h, t */
+  void* k_cache;          /* [B, Hkv, capacity, D] */
+  int64_t k_strides[3];
+  void* v_cache;
+  int64_t v_strides[3];
+  int32_t B, T, Hq, Hkv, D, capacity;
+  int32_t pos;
+  const int32_t* pos_dev;
+  float eps;
+} sa_qkv_prologue_args;
+
+SA_API int sa_qk_norm_rope_append(const sa_qkv_prologue_args* args, sa_stream_t stream);
+
+/* Residual add + RMSNorm over rows of n elements (n % 8 == 0, 16-byte aligned rows):
+ *   x = x + y (stored, bf16; y may be NULL), out = x * rsqrt(mean(x^2) + eps) * weight.
+ * Qwen3RMSNorm after each decoder sub-block. */
+SA_API int sa_add_rms_norm(void* x, const void* y, const void* weight, void* out, int64_t rows, int32_t n,
+                           int64_t x_stride, int64_t y_stride, int64_t out_stride, float eps,
+                           sa_stream_t stream);
+
+/* SwiGLU activation: out[r, i] = silu(gu[r, i]) * gu[r, inter + i] (Qwen3MLP act_fn(gate) * up). */
+SA_API int sa_silu_mul(const void* gate_up, void* out, int64_t rows, int32_t inter, int64_t gu_stride,
+                       int64_t out_stride, sa_stream_t stream);
+
 #define SA_DECODE_SCRATCH_FLOATS (4 * 1024 * 1024)
 SA_API int sa_decode_fwd_noalloc(const sa_attn_args* args, int32_t n_split, sa_stream_t stream);
 

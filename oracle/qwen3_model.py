@@ -8,8 +8,9 @@ from MaskedSdpaBackend over the BigBird token mask
 (sparse_attentions/attention/masked_sdpa.py:23-68,
 sparse_attentions/patterns/bigbird_pattern.py:487-531).
 
-``CheckerKernels`` offers the compile_bigbird / prefill_fwd / decode_fwd calls of
-the CUDA ops module computed by this oracle, so that the tensor-parallel host
+``CheckerKernels`` offers the pattern, attention and layer-step calls of the CUDA
+ops module (compile_bigbird, prefill_fwd, decode_fwd, qk_norm_rope_append,
+add_rms_norm, silu_mul) computed by this oracle, so that the tensor-parallel host
 logic can be exercised on CPU ranks (gloo) without a GPU.
 """
 from __future__ import annotations
@@ -111,6 +112,45 @@ class CheckerKernels:
                           block_pair_offsets.cpu().numpy(), block_size)
         if out is None:
             return o.to(q.dtype)
+        out.copy_(o)
+        return out
+
+    @staticmethod
+    def qk_norm_rope_append(qkv, q_weight, k_weight, cos, sin, k_cache, v_cache, *, Hq, Hkv, pos=0, pos_dev=None,
+                            eps=1e-6, q_out=None):
+        p = int(pos_dev.item()) if pos_dev is not None else int(pos)
+        B, T, _, D = qkv.shape
+        x = qkv.float()
+        c = cos[p:p + T].float().view(1, T, 1, D)
+        s = sin[p:p + T].float().view(1, T, 1, D)
+
+        def norm_rope(t, w):
+            t = _rms(t, w.float(), eps)
+            return t * c + torch.cat([-t[..., D // 2:], t[..., : D // 2]], -1) * s
+
+        q = norm_rope(x[:, :, :Hq], q_weight)
+        k = norm_rope(x[:, :, Hq:Hq + Hkv], k_weight)
+        k_cache[:, :, p:p + T] = k.transpose(1, 2).to(k_cache.dtype)
+        v_cache[:, :, p:p + T] = x[:, :, Hq + Hkv:].transpose(1, 2).to(v_cache.dtype)
+        return q.to(qkv.dtype).transpose(1, 2)
+
+    @staticmethod
+    def add_rms_norm(x, y, weight, eps=1e-6, out=None):
+        if y is not None:
+            x += y
+        o = _rms(x.float(), weight.float(), eps).to(x.dtype)
+        if out is None:
+            return o
+        out.copy_(o)
+        return out
+
+    @staticmethod
+    def silu_mul(gate_up, out=None):
+        inter = gate_up.shape[-1] // 2
+        g = gate_up.float()
+        o = (F.silu(g[..., :inter]) * g[..., inter:]).to(gate_up.dtype)
+        if out is None:
+            return o
         out.copy_(o)
         return out
 

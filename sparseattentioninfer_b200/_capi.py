@@ -26,7 +26,11 @@ EXPORTED = (
     "sa_kvlist_pairs",
     "sa_prefill_fwd",
     "sa_decode_fwd",
+    "sa_decode_fwd_seqlen",
     "sa_decode_fwd_noalloc",
+    "sa_qk_norm_rope_append",
+    "sa_add_rms_norm",
+    "sa_silu_mul",
 )
 
 SA_OK = 0
@@ -66,6 +70,16 @@ class AttnArgs(ctypes.Structure):
     ]
 
 
+class QkvPrologueArgs(ctypes.Structure):
+    _fields_ = [
+        ("qkv", _c_p), ("qkv_sb", _c_i64), ("qkv_st", _c_i64), ("q_weight", _c_p), ("k_weight", _c_p),
+        ("cos", _c_p), ("sin", _c_p), ("q_out", _c_p), ("q_strides", _c_i64 * 3), ("k_cache", _c_p),
+        ("k_strides", _c_i64 * 3), ("v_cache", _c_p), ("v_strides", _c_i64 * 3),
+        ("B", _c_i32), ("T", _c_i32), ("Hq", _c_i32), ("Hkv", _c_i32), ("D", _c_i32), ("capacity", _c_i32),
+        ("pos", _c_i32), ("pos_dev", _c_p), ("eps", ctypes.c_float),
+    ]
+
+
 _lib = None
 
 
@@ -94,6 +108,11 @@ def load(path: str | os.PathLike | None = None) -> ctypes.CDLL:
     lib.sa_kvlist_pairs.argtypes = [_c_p, _c_i32, _c_i32, _c_i32, _c_p, _c_p, _c_i32, _c_p]
     lib.sa_prefill_fwd.argtypes = [ctypes.POINTER(AttnArgs), _c_p]
     lib.sa_decode_fwd.argtypes = [ctypes.POINTER(AttnArgs), _c_i32, _c_p, _c_p, _c_p]
+    lib.sa_decode_fwd_seqlen.argtypes = [ctypes.POINTER(AttnArgs), _c_p, _c_i32, _c_p, _c_p, _c_p]
+    lib.sa_qk_norm_rope_append.argtypes = [ctypes.POINTER(QkvPrologueArgs), _c_p]
+    lib.sa_add_rms_norm.argtypes = [_c_p, _c_p, _c_p, _c_p, _c_i64, _c_i32, _c_i64, _c_i64, _c_i64, ctypes.c_float,
+                                    _c_p]
+    lib.sa_silu_mul.argtypes = [_c_p, _c_p, _c_i64, _c_i32, _c_i64, _c_i64, _c_p]
     lib.sa_decode_fwd_noalloc.argtypes = [ctypes.POINTER(AttnArgs), _c_i32, _c_p]
     for name in EXPORTED:
         if name not in ("sa_version", "sa_last_error"):

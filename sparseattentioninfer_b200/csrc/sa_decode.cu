@@ -41,6 +41,7 @@ struct DecodeParams {
   const int32_t* offsets;
   int32_t pairs_stride;
   int32_t B, Hq, Hkv, T_k, bs, n_split, chk;
+  const int32_t* T_k_dev;  // live key count in device memory (<= T_k), or NULL
   float scale_log2;
   float* part_o;   // [B, Hq, n_split, D]
   float* part_ml;  // [B, Hq, n_split, 2]
@@ -123,7 +124,10 @@ __global__ void __launch_bounds__(kDecThreads) decode_split_kernel(const __grid_
   const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int h0 = kvh * G;
-  const int nkb = (p.T_k + p.bs - 1) / p.bs;
+  // Keys [0, T_k): the live length from device memory when given (graph replays
+  // of a growing cache), else the host value; the tensor maps span p.T_k rows.
+  const int T_k = p.T_k_dev ? max(0, min(__ldg(p.T_k_dev), p.T_k)) : p.T_k;
+  const int nkb = (T_k + p.bs - 1) / p.bs;
   const int nwords = (nkb + 3) >> 2;
   DEC_TRACE(0);
 
@@ -223,7 +227,7 @@ __global__ void __launch_bounds__(kDecThreads) decode_split_kernel(const __grid_
         if (i >= kDecStages &&
             !(ok = mbar_wait(smem_u32(&bar_empty[slot]), ((i / kDecStages) - 1) & 1, abort_v, p.err)))
           break;
-        const int key0 = min(stage_key0(i), p.T_k);  // past T_k: zero fill, masked below
+        const int key0 = min(stage_key0(i), T_k);  // past T_k: masked below
         const uint32_t st = sbase + slot * Cfg::kStageBytes;
         mbar_arrive_expect_tx(smem_u32(&bar_full[slot]), 2u * chk * D * 2);
 #pragma unroll
@@ -256,7 +260,7 @@ __global__ void __launch_bounds__(kDecThreads) decode_split_kernel(const __grid_
       bool ok = mbar_wait(smem_u32(&bar_full[slot]), (i / kDecStages) & 1, abort_v, p.err);
       if (!__all_sync(0xffffffffu, ok)) break;
       const int key0 = stage_key0(i);
-      const int rows = max(0, min(chk, p.T_k - key0));
+      const int rows = max(0, min(chk, T_k - key0));
       const uint32_t hm = s_hm[e_begin + i / nsub];
       if (k_lo < rows) {
         const uint32_t sk = sbase + slot * Cfg::kStageBytes;
@@ -459,6 +463,16 @@ extern "C" int sa_decode_fwd(const sa_attn_args* a, int32_t n_split, float* part
   DecodeParams prm;
   int rc = sa_decode_prepare(a, n_split, partial_o, partial_ml, &prm);
   if (rc) return rc;
+  return sa_decode_launch(prm, a, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int sa_decode_fwd_seqlen(const sa_attn_args* a, const int32_t* seq_len, int32_t n_split,
+                                    float* partial_o, float* partial_ml, sa_stream_t stream) {
+  if (!seq_len) return sa_fail(SA_ERR_INVALID, "seq_len is NULL");
+  DecodeParams prm;
+  int rc = sa_decode_prepare(a, n_split, partial_o, partial_ml, &prm);
+  if (rc) return rc;
+  prm.T_k_dev = seq_len;
   return sa_decode_launch(prm, a, reinterpret_cast<cudaStream_t>(stream));
 }
 

@@ -208,9 +208,14 @@ def default_n_split(q: torch.Tensor, k: torch.Tensor) -> int:
 def decode_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, block_pairs: torch.Tensor,
                block_pair_offsets: torch.Tensor, block_size: int, *, scale: float | None = None,
                n_split: int | None = None, out: torch.Tensor | None = None,
-               workspace: tuple[torch.Tensor, torch.Tensor] | None = None) -> torch.Tensor:
+               workspace: tuple[torch.Tensor, torch.Tensor] | None = None,
+               seq_len: torch.Tensor | None = None) -> torch.Tensor:
     """Split-KV sparse decode (T_q == 1): q [B,Hq,1,D], KV cache [B,Hkv,T_k,D] (any
-    T stride, e.g. a view of a larger pre-allocated cache)."""
+    T stride, e.g. a view of a larger pre-allocated cache).
+
+    ``seq_len`` (int32 device tensor, one element): the live key count is read
+    from it on the device and k/v span the capacity, so the call can be captured
+    in a CUDA graph and replayed as the cache grows (sa_decode_fwd_seqlen)."""
     _require_cuda(q, k, v, block_pairs, block_pair_offsets)
     in_dtype = q.dtype
     qb, kb, vb = _as_bf16(q), _as_bf16(k), _as_bf16(v)
@@ -227,12 +232,104 @@ def decode_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, block_pairs: t
             raise ValueError("decode workspace too small")
     a = _fill_args(qb, kb, vb, o, block_pairs, block_pair_offsets, block_size, scale)
     with torch.cuda.device(q.device):
-        _capi.check(_capi.load().sa_decode_fwd(ctypes.byref(a), ns, po.data_ptr(), pml.data_ptr(),
-                                               _stream(q.device)))
+        if seq_len is None:
+            _capi.check(_capi.load().sa_decode_fwd(ctypes.byref(a), ns, po.data_ptr(), pml.data_ptr(),
+                                                   _stream(q.device)))
+        else:
+            _require_cuda(seq_len)
+            if seq_len.dtype != torch.int32 or seq_len.numel() < 1:
+                raise TypeError("seq_len must be an int32 device tensor")
+            _capi.check(_capi.load().sa_decode_fwd_seqlen(ctypes.byref(a), seq_len.data_ptr(), ns, po.data_ptr(),
+                                                          pml.data_ptr(), _stream(q.device)))
     if out is not None and out is not o:
         out.copy_(o)
         return out
     return o if in_dtype == torch.bfloat16 else o.to(in_dtype)
+
+
+
+# ---------------------------------------------------------------------------
+# Decoder-layer steps around attention (sa_layer_ops.cu)
+# ---------------------------------------------------------------------------
+def qk_norm_rope_append(qkv: torch.Tensor, q_weight: torch.Tensor, k_weight: torch.Tensor, cos: torch.Tensor,
+                        sin: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, *, Hq: int, Hkv: int,
+                        pos: int = 0, pos_dev: torch.Tensor | None = None, eps: float = 1e-6,
+                        q_out: torch.Tensor | None = None) -> torch.Tensor:
+    """From qkv [B, T, Hq+2*Hkv, D] (the fused projection output): returns
+    q = RoPE(RMSNorm(q)) [B, Hq, T, D] (a strided view when ``q_out`` is None) and
+    appends RoPE(RMSNorm(k)) and v to the caches [B, Hkv, capacity, D] at
+    positions pos.. (``pos_dev``: int32 device scalar read on the device).
+    The hook's q_norm/k_norm/apply_rotary_pos_emb/cache update
+    (modeling_sparse_qwen3.py:211-231) in one launch."""
+    _require_cuda(qkv, q_weight, k_weight, cos, sin, k_cache, v_cache)
+    B, T, NH, D = qkv.shape
+    if NH != Hq + 2 * Hkv:
+        raise ValueError(f"qkv has {NH} heads, expected {Hq}+2*{Hkv}")
+    if qkv.stride(3) != 1 or qkv.stride(2) != D:
+        raise ValueError("qkv heads must be contiguous [.., heads, D]")
+    for t in (qkv, q_weight, k_weight, cos, sin, k_cache, v_cache):
+        if t.dtype != torch.bfloat16:
+            raise TypeError("bf16 tensors expected")
+    if q_out is None:
+        q_out = torch.empty(B, T, Hq, D, dtype=torch.bfloat16, device=qkv.device).transpose(1, 2)
+    a = _capi.QkvPrologueArgs()
+    a.qkv, a.qkv_sb, a.qkv_st = qkv.data_ptr(), qkv.stride(0), qkv.stride(1)
+    a.q_weight, a.k_weight = q_weight.data_ptr(), k_weight.data_ptr()
+    a.cos, a.sin = cos.data_ptr(), sin.data_ptr()
+    a.q_out, a.k_cache, a.v_cache = q_out.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr()
+    for dst, t in ((a.q_strides, q_out), (a.k_strides, k_cache), (a.v_strides, v_cache)):
+        if t.stride(3) != 1:
+            raise ValueError("last dimension must be contiguous")
+        dst[0], dst[1], dst[2] = t.stride(0), t.stride(1), t.stride(2)
+    a.B, a.T, a.Hq, a.Hkv, a.D, a.capacity = B, T, Hq, Hkv, D, min(k_cache.shape[2], cos.shape[0])
+    a.pos = int(pos)
+    if pos_dev is not None:
+        if pos_dev.dtype != torch.int32:
+            raise TypeError("pos_dev must be int32")
+        a.pos_dev = pos_dev.data_ptr()
+    a.eps = float(eps)
+    with torch.cuda.device(qkv.device):
+        _capi.check(_capi.load().sa_qk_norm_rope_append(ctypes.byref(a), _stream(qkv.device)))
+    return q_out
+
+
+def add_rms_norm(x: torch.Tensor, y: torch.Tensor | None, weight: torch.Tensor, eps: float = 1e-6,
+                 out: torch.Tensor | None = None) -> torch.Tensor:
+    """x += y in place (bf16, y may be None), then returns RMSNorm(x) * weight over
+    the last dimension (Qwen3RMSNorm after a residual add), rows of x [.., n]."""
+    tensors = [x, weight] + ([y] if y is not None else [])
+    _require_cuda(*tensors)
+    n = x.shape[-1]
+    x2 = x.view(-1, n)
+    y2 = y.reshape(-1, n) if y is not None else None
+    if out is None:
+        out = torch.empty_like(x)
+    o2 = out.view(-1, n)
+    for t in tensors + [out]:
+        if t.dtype != torch.bfloat16 or t.stride(-1) != 1:
+            raise TypeError("bf16 tensors with a contiguous last dimension expected")
+    with torch.cuda.device(x.device):
+        _capi.check(_capi.load().sa_add_rms_norm(
+            x2.data_ptr(), y2.data_ptr() if y2 is not None else None, weight.data_ptr(), o2.data_ptr(), x2.shape[0],
+            n, x2.stride(0), y2.stride(0) if y2 is not None else 0, o2.stride(0), float(eps), _stream(x.device)))
+    return out
+
+
+def silu_mul(gate_up: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """silu(gate_up[..., :I]) * gate_up[..., I:] (Qwen3MLP act_fn(gate) * up)."""
+    _require_cuda(gate_up)
+    n = gate_up.shape[-1]
+    inter = n // 2
+    g2 = gate_up.view(-1, n)
+    if out is None:
+        out = torch.empty(*gate_up.shape[:-1], inter, dtype=gate_up.dtype, device=gate_up.device)
+    o2 = out.view(-1, inter)
+    if gate_up.dtype != torch.bfloat16 or out.dtype != torch.bfloat16:
+        raise TypeError("bf16 tensors expected")
+    with torch.cuda.device(gate_up.device):
+        _capi.check(_capi.load().sa_silu_mul(g2.data_ptr(), o2.data_ptr(), g2.shape[0], inter, g2.stride(0),
+                                             o2.stride(0), _stream(gate_up.device)))
+    return out
 
 
 def sparse_attn(q, k, v, block_pairs, block_pair_offsets, block_size: int, *, scale: float | None = None):

@@ -121,34 +121,12 @@ def all_reduce_(t: torch.Tensor, group=None) -> torch.Tensor:
     return t
 
 
-def mlp_block(x: torch.Tensor, L: dict, eps: float, group=None) -> torch.Tensor:
-    """x += down(silu(gate(h)) * up(h)), h = RMSNorm(x); the row-parallel down output
-    is all-reduced before the residual add (modeling_qwen3 Qwen3MLP)."""
-    h = F.rms_norm(x, (x.shape[-1],), L["ln2"], eps)
-    gu = h @ L["gu"].t()
-    inter = gu.shape[-1] // 2
-    y = (F.silu(gu[..., :inter]) * gu[..., inter:]) @ L["down"].t()
-    x += all_reduce_(y, group)
-    return x
-
-
-def o_proj_block(x: torch.Tensor, att: torch.Tensor, L: dict, group=None) -> torch.Tensor:
-    """x += o_proj(att) with att [.., hq_local*D]; all-reduced before the residual add."""
-    x += all_reduce_(att @ L["o"].t(), group)
-    return x
-
-
 def rope_tables(arch: Qwen3Arch, capacity: int, device, dtype=torch.bfloat16):
     D = arch.head_dim
     inv = 1.0 / arch.rope_theta ** (torch.arange(0, D, 2, device=device, dtype=torch.float32) / D)
     ang = torch.outer(torch.arange(capacity, device=device, dtype=torch.float32), inv)
     emb = torch.cat([ang, ang], -1)
     return emb.cos().to(dtype), emb.sin().to(dtype)
-
-
-def _rotate(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
-    D = x.shape[-1]
-    return x * cos + torch.cat([-x[..., D // 2:], x[..., : D // 2]], -1) * sin
 
 
 class Qwen3TPRunner:
@@ -187,6 +165,8 @@ class Qwen3TPRunner:
         self.length = 0
         self._csr = {}
         self._ws = None
+        self._graph = None
+        self._g_csr = {}
 
     # -- CSR -----------------------------------------------------------------
     def _rows(self, pairs, offs):
@@ -220,11 +200,47 @@ class Qwen3TPRunner:
             self._csr[key] = hit
         return hit
 
-    # -- prefill -------------------------------------------------------------
+    # -- one decoder layer ------------------------------------------------------
+    def _layer(self, x: torch.Tensor, h: torch.Tensor, li: int, *, T: int, pos: int, pos_dev, attend,
+               next_norm: torch.Tensor) -> torch.Tensor:
+        """Layer ``li`` on the residual stream x [B, T, hidden] whose RMSNorm(ln1) is
+        h: q/k/v projection, fused q/k norm + RoPE + cache append at positions
+        pos.. (``pos_dev`` on the device), ``attend(li, q) -> att [B, T, hq*D]``,
+        o_proj + all-reduce + residual add + ln2, SwiGLU MLP + all-reduce +
+        residual add, and the next RMSNorm (``next_norm``); returns that."""
+        ops, A, w = self.ops, self.A, self.w
+        L = w.layers[li]
+        B = x.shape[0]
+        D, hq, hkv = A.head_dim, w.hq, w.hkv
+        qkv = (h @ L["qkv"].t()).view(B, T, hq + 2 * hkv, D)
+        q = ops.qk_norm_rope_append(qkv, L["qn"], L["kn"], self.cos, self.sin, self.k_cache[li], self.v_cache[li],
+                                    Hq=hq, Hkv=hkv, pos=pos, pos_dev=pos_dev, eps=A.eps)
+        att = attend(li, q)
+        h = ops.add_rms_norm(x, all_reduce_(att @ L["o"].t(), self.group), L["ln2"], A.eps)
+        act = ops.silu_mul(h @ L["gu"].t())
+        return ops.add_rms_norm(x, all_reduce_(act @ L["down"].t(), self.group), next_norm, A.eps)
+
+    def _forward(self, tok: torch.Tensor, pos: int, pos_dev, attend) -> torch.Tensor:
+        """All layers for tokens [B, T] at positions pos..; returns the final-norm
+        hidden state of the last position [B, hidden]."""
+        A, w = self.A, self.w
+        B, T = tok.shape
+        x = F.embedding(tok, w.embed)  # [B, T, hidden]
+        h = self.ops.add_rms_norm(x, None, w.layers[0]["ln1"], A.eps)
+        for li in range(A.layers):
+            nxt = w.layers[li + 1]["ln1"] if li + 1 < A.layers else w.final_norm
+            h = self._layer(x, h, li, T=T, pos=pos, pos_dev=pos_dev, attend=attend, next_norm=nxt)
+        return h[:, -1]
+
+    def _logits(self, h_last: torch.Tensor) -> torch.Tensor:
+        return (h_last @ self.w.lm_head.t()).float()
+
+    # -- prefill ---------------------------------------------------------------
     @torch.no_grad()
     def prefill(self, tokens: torch.Tensor, chunk: int = 4096) -> torch.Tensor:
         """Run the prompt [B, T] through all layers (filling the cache) and return the
-        last position's logits [B, vocab] (fp32)."""
+        last position's logits [B, vocab] (fp32). Chunks of ``chunk`` positions attend
+        through the CSR rows of their query blocks in the full prompt's CSR."""
         ops = self.ops
         A, w = self.A, self.w
         B, T = tokens.shape
@@ -232,74 +248,161 @@ class Qwen3TPRunner:
             raise ValueError(f"prompt of {T} tokens exceeds the cache capacity {self.capacity}")
         if chunk % self.bs:
             raise ValueError("chunk must be a multiple of the block size")
-        D, hq, hkv = A.head_dim, w.hq, w.hkv
+        D, hq = A.head_dim, w.hq
         csr = {d: self.prefill_csr(T, d) for d in (False, True)
                if (not d and self.sparse) or (d and len(self.sparse) < A.layers)}
-        x_last = None
+        h_last = None
         for c0 in range(0, T, chunk):
             c1 = min(T, c0 + chunk)
             C = c1 - c0
             qb0, qb1 = c0 // self.bs, math.ceil(c1 / self.bs)
-            x = F.embedding(tokens[:, c0:c1], w.embed)  # [B, C, hidden]
-            cos, sin = self.cos[c0:c1].unsqueeze(1), self.sin[c0:c1].unsqueeze(1)  # [C, 1, D]
-            att = torch.empty(B, C, hq, D, device=x.device, dtype=self.dtype)
+            att = torch.empty(B, C, hq, D, device=tokens.device, dtype=self.dtype)
             chunk_offs = {d: offs[:, qb0:qb1 + 1].contiguous() for d, (_, offs) in csr.items()}
-            for li, L in enumerate(w.layers):
-                h = F.rms_norm(x, (A.hidden,), L["ln1"], A.eps)
-                qkv = (h @ L["qkv"].t()).view(B, C, hq + 2 * hkv, D)
-                q = _rotate(F.rms_norm(qkv[:, :, :hq], (D,), L["qn"], A.eps), cos, sin)
-                k = _rotate(F.rms_norm(qkv[:, :, hq:hq + hkv], (D,), L["kn"], A.eps), cos, sin)
-                self.k_cache[li][:, :, c0:c1].copy_(k.transpose(1, 2))
-                self.v_cache[li][:, :, c0:c1].copy_(qkv[:, :, hq + hkv:].transpose(1, 2))
+
+            def attend(li, q, c1=c1, att=att, chunk_offs=chunk_offs):
                 dense = li not in self.sparse
-                pairs = csr[dense][0]
-                ops.prefill_fwd(q.transpose(1, 2), self.k_cache[li][:, :, :c1], self.v_cache[li][:, :, :c1],
-                                pairs, chunk_offs[dense], self.bs, out=att.transpose(1, 2))
-                o_proj_block(x, att.view(B, C, hq * D), L, self.group)
-                mlp_block(x, L, A.eps, self.group)
-            x_last = x[:, -1]
+                ops.prefill_fwd(q, self.k_cache[li][:, :, :c1], self.v_cache[li][:, :, :c1], csr[dense][0],
+                                chunk_offs[dense], self.bs, out=att.transpose(1, 2))
+                return att.view(B, -1, hq * D)
+
+            h_last = self._forward(tokens[:, c0:c1], c0, None, attend)
         self.length = T
-        return self._logits(x_last)
+        return self._logits(h_last)
 
-    def _logits(self, x: torch.Tensor) -> torch.Tensor:
-        h = F.rms_norm(x, (self.A.hidden,), self.w.final_norm, self.A.eps)
-        return (h @ self.w.lm_head.t()).float()
+    # -- decode ----------------------------------------------------------------
+    def _n_split(self) -> int:
+        if self.n_split is not None:
+            return self.n_split
+        return max(1, min(64, math.ceil(self.num_sms / max(1, self.B * self.w.hkv))))
 
-    # -- decode --------------------------------------------------------------
+    def _workspace(self, ns: int, device):
+        B, hq, D = self.B, self.w.hq, self.A.head_dim
+        if self._ws is None or self._ws[0].numel() < B * hq * ns * D:
+            self._ws = (torch.empty(B * hq * ns * D, device=device), torch.empty(B * hq * ns * 2, device=device))
+        return self._ws
+
     @torch.no_grad()
     def step(self, tok: torch.Tensor, return_logits: bool = False):
         """One greedy decode step for tokens [B, 1]; returns the next tokens [B, 1]."""
         ops = self.ops
         A, w = self.A, self.w
         B = tok.shape[0]
-        D, hq, hkv = A.head_dim, w.hq, w.hkv
         pos = self.length
         if pos >= self.capacity:
             raise ValueError("KV cache full")
         T_k = pos + 1
-        cos, sin = self.cos[pos], self.sin[pos]
-        x = F.embedding(tok[:, 0], w.embed)  # [B, hidden]
-        ns = self.n_split if self.n_split is not None else max(1, min(64, math.ceil(self.num_sms / max(1, B * hkv))))
-        if self._ws is None or self._ws[0].numel() < B * hq * ns * D:
-            self._ws = (torch.empty(B * hq * ns * D, device=x.device), torch.empty(B * hq * ns * 2, device=x.device))
-        att = torch.empty(B, hq, 1, D, device=x.device, dtype=self.dtype)
-        for li, L in enumerate(w.layers):
-            h = F.rms_norm(x, (A.hidden,), L["ln1"], A.eps)
-            qkv = (h @ L["qkv"].t()).view(B, hq + 2 * hkv, D)
-            q = _rotate(F.rms_norm(qkv[:, :hq], (D,), L["qn"], A.eps), cos, sin)
-            k = _rotate(F.rms_norm(qkv[:, hq:hq + hkv], (D,), L["kn"], A.eps), cos, sin)
-            self.k_cache[li][:, :, pos].copy_(k)
-            self.v_cache[li][:, :, pos].copy_(qkv[:, hq + hkv:])
+        ns = self._n_split()
+        ws = self._workspace(ns, tok.device)
+        att = torch.empty(B, w.hq, 1, A.head_dim, device=tok.device, dtype=self.dtype)
+
+        def attend(li, q):
             pairs, offs = self.decode_csr(T_k, li not in self.sparse)
-            ops.decode_fwd(q.unsqueeze(2), self.k_cache[li][:, :, :T_k], self.v_cache[li][:, :, :T_k], pairs, offs,
-                           self.bs, n_split=ns, out=att, workspace=self._ws)
-            o_proj_block(x, att.view(B, hq * D), L, self.group)
-            mlp_block(x, L, A.eps, self.group)
+            ops.decode_fwd(q, self.k_cache[li][:, :, :T_k], self.v_cache[li][:, :, :T_k], pairs, offs, self.bs,
+                           n_split=ns, out=att, workspace=ws)
+            return att.view(B, 1, -1)
+
+        logits = self._logits(self._forward(tok, pos, None, attend))
         self.length = T_k
-        logits = self._logits(x)
         nxt = logits.argmax(-1, keepdim=True)
         return (nxt, logits) if return_logits else nxt
 
+    # -- graph-captured decode ---------------------------------------------------
+    def _refresh_graph_csr(self, T_k: int) -> None:
+        for dense, (gp, go) in self._g_csr.items():
+            pairs, offs = self.decode_csr(T_k, dense)
+            gp.zero_()
+            gp[:, : pairs.shape[1]].copy_(pairs)
+            go.copy_(offs)
+
+    @torch.no_grad()
+    def capture_decode(self) -> None:
+        """Record one decode step (all layers, logits, argmax, position advance) in
+        a CUDA graph. The step reads its position and key count from device
+        counters and its CSR from fixed buffers, which ``step_graph`` refreshes
+        when the step enters a new key block; everything else is replayed as is."""
+        ops = self.ops
+        A, w = self.A, self.w
+        dev = w.embed.device
+        B, D = self.B, A.head_dim
+        ns = self._n_split()
+        ws = self._workspace(ns, dev)
+        nkb_cap = math.ceil(self.capacity / self.bs)
+        self._g_csr = {}
+        for dense in (False, True):
+            if (not dense and self.sparse) or (dense and len(self.sparse) < A.layers):
+                width = nkb_cap if dense else sum(self.layout[1:])
+                self._g_csr[dense] = (torch.zeros(w.hq, width, dtype=torch.int32, device=dev),
+                                      torch.zeros(w.hq, 2, dtype=torch.int32, device=dev))
+        self._g_tok = torch.zeros(B, 1, dtype=torch.long, device=dev)
+        self._g_pos = torch.zeros(1, dtype=torch.int32, device=dev)   # position of the fed token
+        self._g_len = torch.zeros(1, dtype=torch.int32, device=dev)   # keys after the append
+        att = torch.empty(B, w.hq, 1, D, device=dev, dtype=self.dtype)
+        # The graph replays into these addresses and holds no reference to them:
+        # the runner keeps every buffer the recorded step touches alive.
+        self._g_keep = (att, ws)
+
+        def attend(li, q):
+            gp, go = self._g_csr[li not in self.sparse]
+            ops.decode_fwd(q, self.k_cache[li], self.v_cache[li], gp, go, self.bs, n_split=ns, out=att,
+                           workspace=ws, seq_len=self._g_len)
+            return att.view(B, 1, -1)
+
+        def body():
+            logits = self._logits(self._forward(self._g_tok, 0, self._g_pos, attend))
+            self._g_tok.copy_(logits.argmax(-1, keepdim=True))
+            self._g_pos.add_(1)
+            self._g_len.add_(1)
+            return logits
+
+        def rewind(p):
+            self._g_pos.fill_(p)
+            self._g_len.fill_(p + 1)
+
+        # warm the body once on a side stream (allocator, library handles), then
+        # rewind the counters and record
+        saved = self.length
+        rewind(saved)
+        self._refresh_graph_csr(saved + 1)
+        s = torch.cuda.Stream(device=dev)
+        s.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(s):
+            body()
+        torch.cuda.current_stream(dev).wait_stream(s)
+        rewind(saved)
+        self._graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self._graph, capture_error_mode="thread_local"):
+            self._g_logits = body()
+        rewind(saved)
+        self._graph_len = saved
+
+    @torch.no_grad()
+    def step_graph(self, tok: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """Replay the captured step. ``tok`` [B, 1] sets the fed token (needed on the
+        first replay; default: the previous replay's argmax, kept on the device).
+        Returns the device buffer holding the next tokens [B, 1] (overwritten by
+        the next replay)."""
+        if self._graph is None:
+            raise RuntimeError("capture_decode() first")
+        pos = self.length
+        if pos >= self.capacity:
+            raise ValueError("KV cache full")
+        moved = pos != self._graph_len  # the host moved the cache (prefill / eager steps)
+        if moved:
+            self._g_pos.fill_(pos)
+            self._g_len.fill_(pos + 1)
+        if pos % self.bs == 0 or moved:
+            self._refresh_graph_csr(pos + 1)
+        if tok is not None:
+            self._g_tok.copy_(tok)
+        self._graph.replay()
+        self.length = self._graph_len = pos + 1
+        return self._g_tok
+
+    @property
+    def graph_logits(self) -> torch.Tensor:
+        """Logits [B, vocab] of the last replay."""
+        return self._g_logits
+
 
 __all__ = ["Qwen3Arch", "QWEN3_4B", "QWEN3_8B", "kv_group_shard", "even_shard", "Qwen3TPWeights",
-           "Qwen3TPRunner", "all_reduce_", "mlp_block", "o_proj_block", "rope_tables"]
+           "Qwen3TPRunner", "all_reduce_", "rope_tables"]
