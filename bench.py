@@ -34,8 +34,16 @@ from pathlib import Path
 
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
-# rank 0's stdout carries exactly one JSON line: NCCL's own messages go to stderr
-os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
+# stdout carries exactly one JSON line: file descriptor 1 is pointed at stderr
+# for the whole run (library messages, e.g. NCCL's version banner, land there)
+# and the result is written to a duplicate of the original stdout.
+_RESULT_FD = os.dup(1)
+os.dup2(2, 1)
+
+
+def emit(line: dict) -> None:
+    sys.stdout.flush()
+    os.write(_RESULT_FD, (json.dumps(line) + "\n").encode())
 
 import torch  # noqa: E402
 
@@ -187,7 +195,7 @@ def run_reference(args) -> None:
                          "sample": f"{per_step_slices} (b,h) slices of S=8192 per step, masked-dense fp32"},
         "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 def time_decode(device) -> dict:
@@ -272,7 +280,7 @@ def time_gqa_layer(device, rank: int, world: int) -> dict:
 
 
 def time_tp_model(device, rank: int, world: int, *, prompt=65536, steps=512, batch=8, chunk=4096,
-                  seed=0) -> dict:
+                  seed=0, use_nvlink_ar=True) -> dict:
     """Config 5: random-init Qwen3-8B architecture (hidden 4096, 36 layers, 32/8
     heads, head_dim 128, SwiGLU 12288, vocab 151936, weights N(0, 0.02)) in bf16,
     tensor-parallel over the KV groups (sparseattentioninfer_b200.tp; NCCL
@@ -283,7 +291,11 @@ def time_tp_model(device, rank: int, world: int, *, prompt=65536, steps=512, bat
     from sparseattentioninfer_b200 import tp
     torch.cuda.empty_cache()
     w = tp.Qwen3TPWeights(tp.QWEN3_8B, rank, world, seed=seed, device=device)
-    runner = tp.Qwen3TPRunner(w, batch, prompt + steps + 64, (128, 2, 4, 3))
+    comm = None
+    if world > 1 and use_nvlink_ar:
+        from sparseattentioninfer_b200.comm import NvlinkAllReduce
+        comm = NvlinkAllReduce(batch * tp.QWEN3_8B.hidden * 2, device=device)  # decode messages
+    runner = tp.Qwen3TPRunner(w, batch, prompt + steps + 64, (128, 2, 4, 3), comm=comm)
     tok = torch.randint(0, tp.QWEN3_8B.vocab, (batch, prompt), generator=torch.Generator().manual_seed(5))
     tok = tok.to(device)
 
@@ -331,10 +343,15 @@ def time_tp_model(device, rank: int, world: int, *, prompt=65536, steps=512, bat
            "ttft_s": ttft, "prefill_tok_s": batch * prompt / ttft, "decode_tok_s": batch * steps / dec,
            "decode_ms_per_step": dec / steps * 1e3, "decode": "CUDA graph per step (captured once)",
            "decode_eager_tok_s": batch * eager_steps / dec_eager, "n_gpus": world,
-           "collective": "NCCL all-reduce (bf16 sum) after o_proj and down_proj" if world > 1 else "none",
+           "collective": ("none" if world == 1 else
+                          "decode: fused NVLink peer-memory all-reduce + residual add + RMSNorm (one kernel) after "
+                          "o_proj and down_proj; prefill: NCCL all-reduce" if comm is not None else
+                          "NCCL all-reduce (bf16 sum) after o_proj and down_proj"),
            "weights": "random N(0,0.02), drawn per full matrix then sliced (same model at every N)",
            "last_token": last}
     del runner, w, logits
+    if comm is not None:
+        comm.close()
     torch.cuda.empty_cache()
     return res
 
@@ -574,7 +591,7 @@ def run_ours(args) -> None:
         line["cpu_baseline"] = {"value": rate, "unit": "TFLOP/s", "cores": threads, "kind": "port",
                                 "sample": f"{done} (b,h) slices of S=8192 (masked-dense fp32, reference "
                                           f"algorithm restated), {wall:.1f} s"}
-    print(json.dumps(line), flush=True)
+    emit(line)
     if world > 1:
         torch.distributed.destroy_process_group()
 

@@ -12,6 +12,7 @@
 #ifndef SPARSE_ATTN_B200_H
 #define SPARSE_ATTN_B200_H
 
+#include <stddef.h>
 #include <stdint.h>
 
 #if defined(__GNUC__)
@@ -243,6 +244,42 @@ SA_API int sa_add_rms_norm(void* x, const void* y, const void* weight, void* out
 /* SwiGLU activation: out[r, i] = silu(gu[r, i]) * gu[r, inter + i] (Qwen3MLP act_fn(gate) * up). */
 SA_API int sa_silu_mul(const void* gate_up, void* out, int64_t rows, int32_t inter, int64_t gu_stride,
                        int64_t out_stride, sa_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * Tensor-parallel all-reduce over NVLink peer memory, fused with the residual
+ * add and the next RMSNorm (no counterpart in the reference, which runs on one
+ * device; it replaces the NCCL all-reduce after o_proj / down_proj for small,
+ * latency-bound decode messages).
+ *
+ * Buffers: each rank allocates with sa_ar_alloc a data region (two slots of
+ * rows*n bf16 each) and a flag region (max_ctas * SA_AR_MAX_WORLD uint32), shares
+ * them with sa_ar_ipc_handle / sa_ar_ipc_open, and keeps max_ctas uint32 epoch
+ * counters in its own memory (zeroed). Every rank writes its partial sum
+ * y_rank [rows, n] (contiguous) at data[rank] + data_offset, then calls
+ * sa_allreduce_add_rms_norm with the same arguments on every rank:
+ *   x += y_0 + ... + y_{world-1}   (fp32 sum in rank order, stored bf16),
+ *   out = x * rsqrt(mean(x^2) + eps) * weight.
+ * Consecutive calls must alternate between the two slots. Waits for peers are
+ * bounded (2 s); on expiry the device error word reads SA_DEV_ERR_TIMEOUT and x
+ * is left unchanged. Plain loads/stores to peer memory only (no multicast).
+ * ------------------------------------------------------------------------- */
+#define SA_AR_MAX_WORLD 8
+typedef struct sa_ar_peers {
+  int32_t rank, world;
+  void* data[SA_AR_MAX_WORLD];       /* each rank's data region (own and peers' mappings) */
+  uint32_t* flags[SA_AR_MAX_WORLD];  /* each rank's flag region */
+  uint32_t* epoch;                   /* this rank's counters [max_ctas] */
+  int32_t max_ctas;
+} sa_ar_peers;
+
+SA_API int sa_ar_alloc(size_t bytes, void** ptr);
+SA_API int sa_ar_free(void* ptr);
+SA_API int sa_ar_ipc_handle(void* ptr, void* handle /* 64 bytes */);
+SA_API int sa_ar_ipc_open(const void* handle /* 64 bytes */, void** ptr);
+SA_API int sa_ar_ipc_close(void* ptr);
+SA_API int sa_allreduce_add_rms_norm(const sa_ar_peers* peers, int64_t data_offset, void* x, const void* weight,
+                                     void* out, int64_t rows, int32_t n, int64_t x_stride, int64_t out_stride,
+                                     float eps, sa_stream_t stream);
 
 #define SA_DECODE_SCRATCH_FLOATS (4 * 1024 * 1024)
 SA_API int sa_decode_fwd_noalloc(const sa_attn_args* args, int32_t n_split, sa_stream_t stream);

@@ -31,6 +31,12 @@ EXPORTED = (
     "sa_qk_norm_rope_append",
     "sa_add_rms_norm",
     "sa_silu_mul",
+    "sa_ar_alloc",
+    "sa_ar_free",
+    "sa_ar_ipc_handle",
+    "sa_ar_ipc_open",
+    "sa_ar_ipc_close",
+    "sa_allreduce_add_rms_norm",
 )
 
 SA_OK = 0
@@ -80,6 +86,11 @@ class QkvPrologueArgs(ctypes.Structure):
     ]
 
 
+class ArPeers(ctypes.Structure):
+    _fields_ = [("rank", _c_i32), ("world", _c_i32), ("data", _c_p * 8), ("flags", _c_p * 8), ("epoch", _c_p),
+                ("max_ctas", _c_i32)]
+
+
 _lib = None
 
 
@@ -113,6 +124,13 @@ def load(path: str | os.PathLike | None = None) -> ctypes.CDLL:
     lib.sa_add_rms_norm.argtypes = [_c_p, _c_p, _c_p, _c_p, _c_i64, _c_i32, _c_i64, _c_i64, _c_i64, ctypes.c_float,
                                     _c_p]
     lib.sa_silu_mul.argtypes = [_c_p, _c_p, _c_i64, _c_i32, _c_i64, _c_i64, _c_p]
+    lib.sa_ar_alloc.argtypes = [ctypes.c_size_t, ctypes.POINTER(_c_p)]
+    lib.sa_ar_free.argtypes = [_c_p]
+    lib.sa_ar_ipc_handle.argtypes = [_c_p, _c_p]
+    lib.sa_ar_ipc_open.argtypes = [_c_p, ctypes.POINTER(_c_p)]
+    lib.sa_ar_ipc_close.argtypes = [_c_p]
+    lib.sa_allreduce_add_rms_norm.argtypes = [ctypes.POINTER(ArPeers), _c_i64, _c_p, _c_p, _c_p, _c_i64, _c_i32,
+                                              _c_i64, _c_i64, ctypes.c_float, _c_p]
     lib.sa_decode_fwd_noalloc.argtypes = [ctypes.POINTER(AttnArgs), _c_i32, _c_p]
     for name in EXPORTED:
         if name not in ("sa_version", "sa_last_error"):

@@ -139,8 +139,11 @@ class Qwen3TPRunner:
 
     def __init__(self, weights: Qwen3TPWeights, batch: int, capacity: int, layout: Sequence[int],
                  *, sparse_layers: Optional[Sequence[int]] = None, group=None, n_split: Optional[int] = None,
-                 kernels=None):
+                 kernels=None, comm=None):
         self.w = weights
+        # ``comm`` (comm.NvlinkAllReduce): messages that fit its slots take the
+        # fused NVLink all-reduce + add + RMSNorm kernel instead of NCCL.
+        self.comm = comm
         if kernels is None:
             from . import ops as kernels
         # ``kernels`` supplies compile_bigbird / prefill_fwd / decode_fwd with the
@@ -216,6 +219,13 @@ class Qwen3TPRunner:
         q = ops.qk_norm_rope_append(qkv, L["qn"], L["kn"], self.cos, self.sin, self.k_cache[li], self.v_cache[li],
                                     Hq=hq, Hkv=hkv, pos=pos, pos_dev=pos_dev, eps=A.eps)
         att = attend(li, q)
+        if self.comm is not None and self.comm.fits(B * T * A.hidden):
+            shape = (B, T, A.hidden)
+            torch.matmul(att, L["o"].t(), out=self.comm.buffer(0, shape))
+            h = self.comm.add_rms_norm(0, x, L["ln2"], A.eps)
+            act = ops.silu_mul(h @ L["gu"].t())
+            torch.matmul(act, L["down"].t(), out=self.comm.buffer(1, shape))
+            return self.comm.add_rms_norm(1, x, next_norm, A.eps)
         h = ops.add_rms_norm(x, all_reduce_(att @ L["o"].t(), self.group), L["ln2"], A.eps)
         act = ops.silu_mul(h @ L["gu"].t())
         return ops.add_rms_norm(x, all_reduce_(act @ L["down"].t(), self.group), next_norm, A.eps)
