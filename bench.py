@@ -361,85 +361,85 @@ def time_tp_model(device, rank: int, world: int, *, prompt=65536, steps=512, bat
 def time_qwen3_decode(device, layers=36, batch=32, ctx=32768, steps=256, chunk=1024, sparse_layers=18,
                       seed=0) -> dict:
     """Config 4: random-init Qwen3-4B architecture (hidden 2560, 36 layers, 32/8 heads,
-    head_dim 128, SwiGLU 9728, vocab 151936, RoPE 1e6, weights N(0,0.02)) in bf16,
-    batch 32, KV cache prefilled (chunked) from 32768 uniform-random token ids,
-    BigBird (64, 2, 4, 2) in layers 0..17, layers 18..35 dense; then `steps`
-    greedy decode steps through the lean runner (runtime.Qwen3DecodeRunner; the
-    prefill runs through the HF model with the hook). Arm "sparse": sparse layers
-    on the split-KV decode kernel, dense layers on PyTorch SDPA; arm
-    "sparse_own_dense": dense layers on the decode kernel too; arm "dense": every
-    layer on PyTorch SDPA (the dense FlashAttention comparator). Both arms decode from the same prefilled cache (decode cost does
-    not depend on the cached values). Timing: CUDA events around the decode
-    loop (host overhead of the HF model included, per-step argmax on device)."""
-    from transformers import Qwen3Config, Qwen3ForCausalLM
-    from sparseattentioninfer_b200 import qwen3 as sq
-    sq.register_attention_implementation()
-    cfg = Qwen3Config(vocab_size=151936, hidden_size=2560, intermediate_size=9728, num_hidden_layers=layers,
-                      num_attention_heads=32, num_key_value_heads=8, head_dim=128, rope_theta=1e6,
-                      max_position_embeddings=ctx + steps + 16, tie_word_embeddings=True, initializer_range=0.02)
-    cfg._attn_implementation = "cuda_sm100"
-    cfg.sparse_attention_dense_impl = "sdpa"
-    torch.manual_seed(seed)
-    with torch.device(device):
-        model = Qwen3ForCausalLM(cfg).to(torch.bfloat16).eval()
-    layer_layouts = [[(64, 2, 4, 2)]] * sparse_layers + [None] * (layers - sparse_layers)
-    sq.replace_qwen3_attention_with_sparse(model, layer_layouts=layer_layouts)
-    for l in model.model.layers:
-        l.self_attn.collect_pattern_stats = False
-    cache = sq.PreallocatedKVCache(layers, ctx + steps + 8)
+    head_dim 128, SwiGLU 9728, vocab 151936, tied embeddings, RoPE 1e6, weights
+    N(0,0.02), norms 1) in bf16, batch 32, KV cache prefilled (chunked) from 32768
+    uniform-random token ids, BigBird (64, 2, 4, 2) in layers 0..17, layers 18..35
+    dense; then `steps` greedy decode steps through sparseattentioninfer_b200.tp
+    (one rank). Arms, all decoding from the same prefilled cache (decode cost does
+    not depend on the cached values):
+      sparse      layers 0..17 on the sparse decode kernel, 18..35 dense on the same
+                  kernel over a dense CSR; one CUDA graph per step;
+      dense       every layer dense on the same engine (the same-engine dense path);
+      dense_sdpa  every layer dense on PyTorch SDPA (cuDNN flash attention, the
+                  fastest dense library decode measured here), eager; a warm pass
+                  over the same lengths caches cuDNN's per-length plans first.
+    Timing: CUDA events around the decode loop; argmax on the device."""
+    import dataclasses
+    from sparseattentioninfer_b200 import tp
+    arch = dataclasses.replace(tp.QWEN3_4B, layers=layers)
+    torch.cuda.empty_cache()
+    w = tp.Qwen3TPWeights(arch, 0, 1, seed=seed, device=device)
+    runner = tp.Qwen3TPRunner(w, batch, ctx + steps + 8, (64, 2, 4, 2), sparse_layers=range(sparse_layers))
     g = torch.Generator(device=device).manual_seed(seed + 1)
-    ids = torch.randint(0, cfg.vocab_size, (batch, ctx), generator=g, device=device)
+    ids = torch.randint(0, arch.vocab, (batch, ctx), generator=g, device=device)
     out = {"workload": f"qwen3_4b_arch_b{batch}_ctx{ctx}_bigbird64_2_4_2_layers0-{sparse_layers - 1}",
            "layers": layers, "batch": batch, "ctx": ctx, "steps": steps}
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    logits = runner.prefill(ids, chunk=chunk)
+    first = logits.argmax(-1, keepdim=True)
+    torch.cuda.synchronize()
+    out["prefill_s"] = time.perf_counter() - t0
+    del logits
+
+    def graph_arm(n):
+        runner.length = ctx
+        runner.capture_decode()
+        runner.step_graph(first)
+        for _ in range(7):
+            runner.step_graph()
+        runner.length = ctx
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        runner.step_graph(first)
+        for _ in range(n - 1):
+            runner.step_graph()
+        e1.record()
+        torch.cuda.synchronize()
+        runner._graph = None
+        return e0.elapsed_time(e1) / 1e3
+
+    def eager_arm(n):
+        tok = first
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(n):
+            tok = runner.step(tok)
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / 1e3
+
     with torch.no_grad():
-        torch.cuda.synchronize()
-        t0 = time.perf_counter()
-        logits = None
-        for c in range(0, ctx, chunk):
-            logits = model(ids[:, c:c + chunk], past_key_values=cache, use_cache=True, logits_to_keep=1).logits
-        torch.cuda.synchronize()
-        out["prefill_s"] = time.perf_counter() - t0
-        first = logits[:, -1].argmax(-1, keepdim=True)
-
-        from sparseattentioninfer_b200.runtime import Qwen3DecodeRunner
-
-        def decode(runner, n):
-            tok = first
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            for i in range(n + 3):
-                if i == 3:
-                    e0.record()
-                tok = runner.step(tok)
-            e1.record()
-            torch.cuda.synchronize()
-            return e0.elapsed_time(e1) / 1e3
-
-        def rewind():
-            for layer in cache.layers:
-                layer.length = ctx
-
-        # Each arm runs twice over the same lengths and the second pass is timed:
-        # PyTorch SDPA (cuDNN) builds an execution plan per new KV length (~25 ms
-        # of host time), which the warm pass caches, for both arms alike.
-        arms = {"sparse": Qwen3DecodeRunner(model, cache, layer_layouts, dense_impl="sdpa"),
-                "sparse_own_dense": Qwen3DecodeRunner(model, cache, layer_layouts, dense_impl="cuda_sm100"),
-                "dense": Qwen3DecodeRunner(model, cache, [None] * layers, dense_impl="sdpa")}
-        times = {}
-        for name, runner in arms.items():
-            rewind()
-            decode(runner, steps)
-            rewind()
-            times[name] = decode(runner, steps)
-        t_sparse, t_dense = times["sparse"], times["dense"]
-        out["sparse_own_dense_tok_s"] = batch * steps / times["sparse_own_dense"]
-    out["sparse_tok_s"] = batch * steps / t_sparse
-    out["dense_tok_s"] = batch * steps / t_dense
-    out["sparse_ms_per_step"] = t_sparse / steps * 1e3
-    out["dense_ms_per_step"] = t_dense / steps * 1e3
-    out["speedup_vs_dense_sdpa"] = t_dense / t_sparse
-    del model, cache
+        t_sparse = graph_arm(steps)
+        runner.sparse = set()
+        t_dense = graph_arm(steps)
+        runner.dense_impl = "sdpa"
+        runner.length = ctx
+        eager_arm(steps)  # warm: cuDNN plans for every length
+        runner.length = ctx
+        t_sdpa = eager_arm(steps)
+    out.update({
+        "sparse_tok_s": batch * steps / t_sparse, "dense_tok_s": batch * steps / t_dense,
+        "dense_sdpa_tok_s": batch * steps / t_sdpa,
+        "sparse_ms_per_step": t_sparse / steps * 1e3, "dense_ms_per_step": t_dense / steps * 1e3,
+        "dense_sdpa_ms_per_step": t_sdpa / steps * 1e3,
+        "speedup_vs_dense": t_dense / t_sparse, "speedup_vs_dense_sdpa": t_sdpa / t_sparse,
+        "decode": "sparse and dense: one CUDA graph per step; dense_sdpa: eager",
+    })
+    del runner, w
     torch.cuda.empty_cache()
     return out
+
 
 def run_ours(args) -> None:
     world, rank, local = dist_env()

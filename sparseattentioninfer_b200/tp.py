@@ -139,8 +139,15 @@ class Qwen3TPRunner:
 
     def __init__(self, weights: Qwen3TPWeights, batch: int, capacity: int, layout: Sequence[int],
                  *, sparse_layers: Optional[Sequence[int]] = None, group=None, n_split: Optional[int] = None,
-                 kernels=None, comm=None):
+                 kernels=None, comm=None, dense_impl: str = "cuda_sm100"):
         self.w = weights
+        # dense layers: "cuda_sm100" (this package's kernels over a dense CSR;
+        # graph-capturable) or "sdpa" (PyTorch SDPA, the library comparator; eager
+        # decode only, its causal mask is top-left aligned so prefill stays on
+        # the package's kernel)
+        if dense_impl not in ("cuda_sm100", "sdpa"):
+            raise ValueError(dense_impl)
+        self.dense_impl = dense_impl
         # ``comm`` (comm.NvlinkAllReduce): messages that fit its slots take the
         # fused NVLink all-reduce + add + RMSNorm kernel instead of NCCL.
         self.comm = comm
@@ -306,9 +313,11 @@ class Qwen3TPRunner:
         att = torch.empty(B, w.hq, 1, A.head_dim, device=tok.device, dtype=self.dtype)
 
         def attend(li, q):
+            kc, vc = self.k_cache[li][:, :, :T_k], self.v_cache[li][:, :, :T_k]
+            if li not in self.sparse and self.dense_impl == "sdpa":
+                return F.scaled_dot_product_attention(q, kc, vc, enable_gqa=True).view(B, 1, -1)
             pairs, offs = self.decode_csr(T_k, li not in self.sparse)
-            ops.decode_fwd(q, self.k_cache[li][:, :, :T_k], self.v_cache[li][:, :, :T_k], pairs, offs, self.bs,
-                           n_split=ns, out=att, workspace=ws)
+            ops.decode_fwd(q, kc, vc, pairs, offs, self.bs, n_split=ns, out=att, workspace=ws)
             return att.view(B, 1, -1)
 
         logits = self._logits(self._forward(tok, pos, None, attend))
@@ -330,6 +339,8 @@ class Qwen3TPRunner:
         a CUDA graph. The step reads its position and key count from device
         counters and its CSR from fixed buffers, which ``step_graph`` refreshes
         when the step enters a new key block; everything else is replayed as is."""
+        if self.dense_impl == "sdpa" and len(self.sparse) < self.A.layers:
+            raise RuntimeError("dense_impl='sdpa' cannot be captured (its length is a host value)")
         ops = self.ops
         A, w = self.A, self.w
         dev = w.embed.device
