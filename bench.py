@@ -562,7 +562,12 @@ def run_ours(args) -> None:
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                      "frac": achieved / peak, "peak_kind": f"{peak_kind} bf16 dense (burst)",
                      "traffic": traffic_from_profile("prefill_cfg2_ncu.txt"),
-                     "kernel": "sa::prefill_kernel<128,64,2>", "traffic_note": "ncu dram read+write of one launch, profiles/prefill_cfg2_ncu.txt", "launch_ms": t_launch * 1e3},
+                     "kernel": "sa::prefill_kernel<128,64,2>", "traffic_note": "ncu dram read+write of one launch, profiles/prefill_cfg2_ncu.txt", "launch_ms": t_launch * 1e3,
+                     "sustained": {"achieved": value / max(1, world),
+                                   "peak": float(peaks.get("bf16_tflops_sustained", 1400.0)),
+                                   "frac": value / max(1, world) / float(peaks.get("bf16_tflops_sustained", 1400.0)),
+                                   "note": "per-GPU throughput of the K back-to-back steps against the "
+                                           "sustained (power-capped) cuBLAS figure"}},
         "e2e": {"value": total_flops * e2e_steps / e2e_elapsed / 1e12, "unit": "TFLOP/s",
                 "h2d_bytes_per_step": in_bytes, "d2h_bytes_per_step": q.numel() * 2,
                 "ms_per_step": e2e_elapsed / e2e_steps * 1e3,
