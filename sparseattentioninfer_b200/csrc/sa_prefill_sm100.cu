@@ -470,7 +470,9 @@ __global__ void __launch_bounds__(LANES * 192, CTAS) prefill_kernel(const __grid
       bool first = true;
       while (true) {
         const int ms = g % kMetaRing;
+        if (L == 0 && threadIdx.x == 64) SA_TRACE(g, 8);
         ok = mbar_wait(smem_u32(&bar_meta[L][ms]), (g / kMetaRing) & 1, abort_v, p.err);
+        if (L == 0 && threadIdx.x == 64) SA_TRACE(g, 9);
         if (!__all_sync(FULL, ok)) { ok = false; break; }
         const int key0 = meta_key0[L][ms];
         const uint32_t mask = meta_mask[L][ms];
