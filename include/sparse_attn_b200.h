@@ -246,6 +246,29 @@ SA_API int sa_silu_mul(const void* gate_up, void* out, int64_t rows, int32_t int
                        int64_t out_stride, sa_stream_t stream);
 
 /* ---------------------------------------------------------------------------
+ * Data-dependent top-k attention (TopKPattern; MaskedSdpaBackend's "topk" kind,
+ * masked_sdpa.py:51-63), second half: given fp32 scores q.k^T.scale of a block
+ * of query rows (a [B, Hkv, G * rows_per_head, T_k] GEMM output, row stride
+ * s_row, for query positions [t0, t0 + rows_per_head)), masks each row causally
+ * (bottom-right aligned) in place, keeps its top_k scores, and writes
+ * out[b, h, t] = softmax(kept) . V with h = kv_head * G + g. v is bf16
+ * [B, Hkv, T_k, D] (element strides); out is bf16, or fp32 with out_f32.
+ * Scores tied exactly at the k-th value are all kept. D in {64, 128}.
+ * ------------------------------------------------------------------------- */
+typedef struct sa_topk_args {
+  void* scores;
+  int64_t s_row;
+  const void* v;
+  int64_t v_strides[3];
+  void* out;
+  int64_t o_strides[3];
+  int32_t out_f32;
+  int32_t B, Hkv, G, rows_per_head, t0, T_q, T_k, D, top_k;
+} sa_topk_args;
+
+SA_API int sa_topk_softmax_pv(const sa_topk_args* args, sa_stream_t stream);
+
+/* ---------------------------------------------------------------------------
  * Tensor-parallel all-reduce over NVLink peer memory, fused with the residual
  * add and the next RMSNorm (no counterpart in the reference, which runs on one
  * device; it replaces the NCCL all-reduce after o_proj / down_proj for small,

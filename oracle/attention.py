@@ -120,4 +120,20 @@ def csr_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, pairs: np.n
     return out
 
 
-__all__ = ["masked_sdpa", "masked_sdpa_chunked", "csr_attention", "token_mask_from_csr"]
+
+def topk_sdpa(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, top_k: int) -> torch.Tensor:
+    """MaskedSdpaBackend.forward for kind "topk" (masked_sdpa.py:51-63): causal
+    mask first (last row for decode), then torch.topk of each score row, softmax
+    over the kept entries, times V. q [B,H,T_q,D]; k/v with H heads (repeated)."""
+    q, k, v = q.float(), k.float(), v.float()
+    D = q.size(-1)
+    T_q, T_k = q.size(2), k.size(2)
+    top = min(top_k, T_k)
+    scores = torch.matmul(q, k.transpose(-2, -1)) * (1.0 / math.sqrt(D))
+    scores = scores.masked_fill(~_causal_keep(T_q, T_k).unsqueeze(0).unsqueeze(0), float("-inf"))
+    vals, idx = torch.topk(scores, k=top, dim=-1)
+    sparse = torch.full_like(scores, float("-inf")).scatter_(-1, idx, vals)
+    attn = torch.nan_to_num(torch.softmax(sparse, dim=-1), nan=0.0)
+    return torch.matmul(attn, v)
+
+__all__ = ["masked_sdpa", "masked_sdpa_chunked", "csr_attention", "topk_sdpa", "token_mask_from_csr"]

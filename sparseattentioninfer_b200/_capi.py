@@ -31,6 +31,7 @@ EXPORTED = (
     "sa_qk_norm_rope_append",
     "sa_add_rms_norm",
     "sa_silu_mul",
+    "sa_topk_softmax_pv",
     "sa_ar_alloc",
     "sa_ar_free",
     "sa_ar_ipc_handle",
@@ -86,6 +87,13 @@ class QkvPrologueArgs(ctypes.Structure):
     ]
 
 
+class TopkArgs(ctypes.Structure):
+    _fields_ = [("scores", _c_p), ("s_row", _c_i64), ("v", _c_p), ("v_strides", _c_i64 * 3), ("out", _c_p),
+                ("o_strides", _c_i64 * 3), ("out_f32", _c_i32), ("B", _c_i32), ("Hkv", _c_i32), ("G", _c_i32),
+                ("rows_per_head", _c_i32), ("t0", _c_i32), ("T_q", _c_i32), ("T_k", _c_i32), ("D", _c_i32),
+                ("top_k", _c_i32)]
+
+
 class ArPeers(ctypes.Structure):
     _fields_ = [("rank", _c_i32), ("world", _c_i32), ("data", _c_p * 8), ("flags", _c_p * 8), ("epoch", _c_p),
                 ("max_ctas", _c_i32)]
@@ -124,6 +132,7 @@ def load(path: str | os.PathLike | None = None) -> ctypes.CDLL:
     lib.sa_add_rms_norm.argtypes = [_c_p, _c_p, _c_p, _c_p, _c_i64, _c_i32, _c_i64, _c_i64, _c_i64, ctypes.c_float,
                                     _c_p]
     lib.sa_silu_mul.argtypes = [_c_p, _c_p, _c_i64, _c_i32, _c_i64, _c_i64, _c_p]
+    lib.sa_topk_softmax_pv.argtypes = [ctypes.POINTER(TopkArgs), _c_p]
     lib.sa_ar_alloc.argtypes = [ctypes.c_size_t, ctypes.POINTER(_c_p)]
     lib.sa_ar_free.argtypes = [_c_p]
     lib.sa_ar_ipc_handle.argtypes = [_c_p, _c_p]

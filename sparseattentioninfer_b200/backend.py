@@ -42,7 +42,8 @@ class CudaSm100Backend(AttentionBackend):
         on the device first (build_block_pairs_from_mask semantics);
       * "dense": full causal attention through a dense causal CSR (block 128) —
         bottom-right aligned, so decode is correct (unlike dense_sdpa.py:24);
-      * "topk": data-dependent, not implemented by this backend (raises).
+      * "topk": data-dependent top-k per query row (``ops.topk_attention``:
+        fp32 score GEMM, then masking, selection, softmax and PV in one kernel).
     """
 
     name = "cuda_sm100"
@@ -89,6 +90,9 @@ class CudaSm100Backend(AttentionBackend):
                 pairs, offsets = self._mask_cache[key]
             if bs is None:
                 raise ValueError("pattern.block_size is None")
+        elif pattern.kind == "topk":
+            self._last = "cuda_sm100"
+            return _ops.topk_attention(q, k, v, int(pattern.topk))
         else:
             raise NotImplementedError(f"cuda_sm100 does not implement pattern kind {pattern.kind!r}")
         self._last = "cuda_sm100"

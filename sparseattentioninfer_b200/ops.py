@@ -332,6 +332,47 @@ def silu_mul(gate_up: torch.Tensor, out: torch.Tensor | None = None) -> torch.Te
     return out
 
 
+
+def topk_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, top_k: int, *, scale: float | None = None,
+                   max_score_bytes: int = 1 << 29) -> torch.Tensor:
+    """Data-dependent top-k attention (the reference's TopKPattern through
+    MaskedSdpaBackend, masked_sdpa.py:51-63): per query row, the causal scores'
+    top_k entries go through softmax and weight V. Scores are an fp32 GEMM of
+    the (bf16-valued) inputs, query rows in chunks of at most
+    ``max_score_bytes`` of scores; masking, selection, softmax and the gathered
+    PV product are sa_topk_softmax_pv. GQA reads K/V head h // (Hq/Hkv)."""
+    _require_cuda(q, k, v)
+    B, Hq, T_q, D = q.shape
+    Hkv, T_k = k.shape[1], k.shape[2]
+    if Hq % Hkv:
+        raise ValueError(f"Hq={Hq} is not a multiple of Hkv={Hkv}")
+    if T_q > T_k:
+        raise ValueError("T_q must not exceed T_k")
+    G = Hq // Hkv
+    sc = float(scale) if scale is not None else 1.0 / math.sqrt(D)
+    qf, kf = q.float(), k.float()
+    vb = _as_bf16(v)
+    out_f32 = q.dtype == torch.float32
+    out = torch.empty(B, Hq, T_q, D, dtype=torch.float32 if out_f32 else torch.bfloat16, device=q.device)
+    rows = max(1, min(T_q, max_score_bytes // max(1, B * Hq * T_k * 4)))
+    lib = _capi.load()
+    for t0 in range(0, T_q, rows):
+        rc = min(rows, T_q - t0)
+        qc = qf[:, :, t0:t0 + rc].reshape(B, Hkv, G * rc, D)
+        scores = torch.matmul(qc, kf.transpose(-1, -2)).mul_(sc).contiguous()
+        a = _capi.TopkArgs()
+        a.scores, a.s_row = scores.data_ptr(), T_k
+        a.v = vb.data_ptr()
+        a.v_strides[0], a.v_strides[1], a.v_strides[2] = vb.stride(0), vb.stride(1), vb.stride(2)
+        a.out = out.data_ptr()
+        a.o_strides[0], a.o_strides[1], a.o_strides[2] = out.stride(0), out.stride(1), out.stride(2)
+        a.out_f32 = int(out_f32)
+        a.B, a.Hkv, a.G, a.rows_per_head, a.t0, a.T_q, a.T_k, a.D, a.top_k = B, Hkv, G, rc, t0, T_q, T_k, D, top_k
+        with torch.cuda.device(q.device):
+            _capi.check(lib.sa_topk_softmax_pv(ctypes.byref(a), _stream(q.device)))
+    return out if q.dtype in (torch.float32, torch.bfloat16) else out.to(q.dtype)
+
+
 def sparse_attn(q, k, v, block_pairs, block_pair_offsets, block_size: int, *, scale: float | None = None):
     """Decode kernel for T_q == 1, tcgen05 prefill kernel otherwise."""
     if q.size(2) == 1:

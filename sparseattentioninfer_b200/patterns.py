@@ -338,13 +338,23 @@ class DenseCausalPattern(SparsePattern):
 
 
 class TopKPattern(SparsePattern):
-    """topk_pattern.py:44-62 (data-dependent; the CUDA backend does not run it)."""
+    """topk_pattern.py:44-62: data-dependent, the backend selects each query row's
+    top_k causal scores (CudaSm100Backend: ops.topk_attention). keep_ratio as
+    the reference computes it (:29-41)."""
 
     def __init__(self, top_k: int):
         self.top_k = top_k
 
     def build(self, q, k, causal: bool = True) -> PatternMetadata:
-        return PatternMetadata(kind="topk", topk=self.top_k)
+        T_q, T_k = q.size(2), k.size(2)
+        top = min(self.top_k, T_k)
+        if T_k <= 0:
+            keep = 0.0
+        elif T_q == T_k:
+            keep = min(1.0, sum(min(top, pos + 1) for pos in range(T_k)) / max(1, T_k * (T_k + 1) // 2))
+        else:
+            keep = min(top, T_k) / T_k
+        return PatternMetadata(kind="topk", topk=self.top_k, keep_ratio=keep)
 
 
 __all__ = [

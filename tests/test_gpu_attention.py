@@ -183,7 +183,7 @@ def test_errors_raise_not_fallback():
     with pytest.raises(_capi.SaError):
         ops.prefill_fwd(q, q, q, pairs, offs, 128)
     with pytest.raises(NotImplementedError):
-        sa.get_backend("cuda_sm100").forward(q, q, q, sa.TopKPattern(8).build(q, q))
+        sa.get_backend("cuda_sm100").forward(q, q, q, sa.PatternMetadata(kind="unknown"))
 
 
 def test_config3_full_size_gqa_layer_heads_vs_oracle():
