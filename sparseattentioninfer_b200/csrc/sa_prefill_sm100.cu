@@ -303,6 +303,7 @@ __global__ void __launch_bounds__(LANES * 192, CTAS) prefill_kernel(const __grid
 #pragma unroll
         for (int r = 0; r < R; ++r)
           tma_load_4d(sQ + r * kTileM * 128, &p.tm_q, smem_u32(&bar_q_full[L]), r * 64, c.q0, c.h, c.b);
+        if (L == 0) SA_TRACE(g, 15);
         ++q_issued;
         ChunkStream cs;
         cs.init(p, c.h, c.qb0, c.nseg, c.nsub);
@@ -404,6 +405,7 @@ __global__ void __launch_bounds__(LANES * 192, CTAS) prefill_kernel(const __grid
         if (!(ok = mbar_wait(smem_u32(&bar_tile[L][it % kTileRing]), (it / kTileRing) & 1, abort_v, p.err))) break;
         if (tile_ring[L][it % kTileRing] < 0) break;
         if (!(ok = mbar_wait(smem_u32(&bar_q_full[L]), it & 1, abort_v, p.err))) break;
+        if (L == 0) SA_TRACE(g, 12);
         tc_fence_after();
         int last = 0;
         const uint32_t g0 = g;
@@ -608,10 +610,12 @@ __global__ void __launch_bounds__(LANES * 192, CTAS) prefill_kernel(const __grid
       if (!ok) break;
       // ---------------------------------------------------------------- epilogue
       ok = mbar_wait(smem_u32(&bar_v_empty[L][(g - 1) % NSV]), ((g - 1) / NSV) & 1, abort_v, p.err);
+      if (L == 0 && threadIdx.x == 64) SA_TRACE(g - 1, 10);
       if (!__all_sync(FULL, ok)) { ok = false; break; }
       tc_fence_after();
       const float inv = l > 0.f ? 1.0f / l : 0.f;
       __nv_bfloat16* orow = p.out + (int64_t)c.b * p.o_sb + (int64_t)c.h * p.o_sh + (int64_t)q_local * p.o_st;
+      const bool out32 = (reinterpret_cast<uintptr_t>(orow) & 31u) == 0;
       uint32_t o32[D / 32][32];
 #pragma unroll
       for (int cc = 0; cc < D / 32; ++cc) tmem_ld32(tmem + lane_base + cc * 32, o32[cc]);
@@ -626,11 +630,20 @@ __global__ void __launch_bounds__(LANES * 192, CTAS) prefill_kernel(const __grid
 #pragma unroll
           for (int i = 0; i < 16; ++i)
             w[i] = pack_bf16(__uint_as_float(o32[cc][2 * i]) * inv, __uint_as_float(o32[cc][2 * i + 1]) * inv);
-          uint4* dst = reinterpret_cast<uint4*>(orow + cc * 32);
+          // One thread owns one row, so every store instruction touches 32 rows:
+          // 256-bit stores write whole 32-byte sectors with half the instructions.
+          __nv_bfloat16* dst = orow + cc * 32;
+          if (out32) {
+            st_global_v8(dst, w);
+            st_global_v8(dst + 16, w + 8);
+          } else {
+            uint4* d4 = reinterpret_cast<uint4*>(dst);
 #pragma unroll
-          for (int i = 0; i < 4; ++i) dst[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+            for (int i = 0; i < 4; ++i) d4[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+          }
         }
       }
+      if (L == 0 && threadIdx.x == 64) SA_TRACE(g - 1, 11);
     }
   }
 
