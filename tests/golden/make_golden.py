@@ -79,7 +79,7 @@ def expand_bitmap(bm: np.ndarray, bs: int, T_q: int, T_k: int) -> torch.Tensor:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True)
     args = ap.parse_args()
     sys.path.insert(0, args.reference)
     from sparse_attentions.attention.masked_sdpa import MaskedSdpaBackend
