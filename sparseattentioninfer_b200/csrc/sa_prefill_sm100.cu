@@ -622,24 +622,75 @@ __global__ void __launch_bounds__(LANES * 192, CTAS) prefill_kernel(const __grid
       tmem_wait_ld();
       tc_fence_before();
       mbar_arrive(smem_u32(&bar_o_empty[L]));  // O is in registers: the next tile may overwrite TMEM
+      if constexpr (D == 128) {
+        // One thread owns one TMEM lane = one row. Pack the row to bf16, then
+        // transpose 64-byte chunks inside each quad of lanes (two shfl_xor
+        // butterfly stages): lane j of quad q ends up with columns [32j, 32j+32)
+        // of rows 4q..4q+3, so a store instruction covers 8 whole rows (full
+        // lines) instead of one 32-byte piece of 32 rows.
+        uint32_t w[4][16];
 #pragma unroll
-      for (int cc = 0; cc < D / 32; ++cc) {
-        reg_fence32(o32[cc]);
-        if (row_ok) {
-          uint32_t w[16];
+        for (int cc = 0; cc < 4; ++cc) {
+          reg_fence32(o32[cc]);
 #pragma unroll
           for (int i = 0; i < 16; ++i)
-            w[i] = pack_bf16(__uint_as_float(o32[cc][2 * i]) * inv, __uint_as_float(o32[cc][2 * i + 1]) * inv);
-          // One thread owns one row, so every store instruction touches 32 rows:
-          // 256-bit stores write whole 32-byte sectors with half the instructions.
-          __nv_bfloat16* dst = orow + cc * 32;
-          if (out32) {
-            st_global_v8(dst, w);
-            st_global_v8(dst + 16, w + 8);
-          } else {
-            uint4* d4 = reinterpret_cast<uint4*>(dst);
+            w[cc][i] = pack_bf16(__uint_as_float(o32[cc][2 * i]) * inv, __uint_as_float(o32[cc][2 * i + 1]) * inv);
+        }
+        const int j = lane & 3;
 #pragma unroll
-            for (int i = 0; i < 4; ++i) d4[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+        for (int b = 0; b < 2; ++b) {
+          const int m = 1 << b;
+          const bool jb = (j >> b) & 1;
+#pragma unroll
+          for (int c0 = 0; c0 < 4; ++c0) {
+            if (c0 & m) continue;
+            const int c1 = c0 | m;
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const uint32_t r = __shfl_xor_sync(FULL, jb ? w[c0][i] : w[c1][i], m);
+              if (jb)
+                w[c0][i] = r;
+              else
+                w[c1][i] = r;
+            }
+          }
+        }
+        const int qd = lane >> 2;
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          const int r_local = c.q0 + wr * 32 + qd * 4 + kk;
+          if (r_local < p.T_q) {
+            __nv_bfloat16* dst =
+                p.out + (int64_t)c.b * p.o_sb + (int64_t)c.h * p.o_sh + (int64_t)r_local * p.o_st + j * 32;
+            if ((reinterpret_cast<uintptr_t>(dst) & 31u) == 0) {
+              st_global_v8(dst, w[kk]);
+              st_global_v8(dst + 16, w[kk] + 8);
+            } else {
+              uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+              for (int i = 0; i < 4; ++i)
+                d4[i] = make_uint4(w[kk][4 * i], w[kk][4 * i + 1], w[kk][4 * i + 2], w[kk][4 * i + 3]);
+            }
+          }
+        }
+      } else {
+#pragma unroll
+        for (int cc = 0; cc < D / 32; ++cc) {
+          reg_fence32(o32[cc]);
+          if (row_ok) {
+            uint32_t w[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+              w[i] = pack_bf16(__uint_as_float(o32[cc][2 * i]) * inv, __uint_as_float(o32[cc][2 * i + 1]) * inv);
+            __nv_bfloat16* dst = orow + cc * 32;
+            if (out32) {
+              st_global_v8(dst, w);
+              st_global_v8(dst + 16, w + 8);
+            } else {
+              uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+              for (int i = 0; i < 4; ++i) d4[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+            }
           }
         }
       }
