@@ -32,6 +32,12 @@
 
 namespace sa {
 
+// Lanes per transpose group of the epilogue stores (4 or 8; 4 measured faster:
+// 997 against 980 TFLOP/s on config 2 in the same run).
+#ifndef SA_EPI_GROUP
+#define SA_EPI_GROUP 4
+#endif
+
 #ifdef SA_PHASE_TRACE
 // Debug-only phase timestamps (clock64) of CTA 0: 16 slots per chunk step.
 __device__ unsigned long long g_sa_trace[16 * 512];
@@ -624,52 +630,56 @@ __global__ void __launch_bounds__(LANES * 192, CTAS) prefill_kernel(const __grid
       mbar_arrive(smem_u32(&bar_o_empty[L]));  // O is in registers: the next tile may overwrite TMEM
       if constexpr (D == 128) {
         // One thread owns one TMEM lane = one row. Pack the row to bf16, then
-        // transpose 64-byte chunks inside each quad of lanes (two shfl_xor
-        // butterfly stages): lane j of quad q ends up with columns [32j, 32j+32)
-        // of rows 4q..4q+3, so a store instruction covers 8 whole rows (full
-        // lines) instead of one 32-byte piece of 32 rows.
-        uint32_t w[4][16];
+        // transpose row chunks inside groups of TG lanes (log2(TG) shfl_xor
+        // butterfly stages): lane j of a group ends up with chunk j of each of
+        // the group's TG rows, so a store instruction writes whole rows of the
+        // group instead of one 32-byte piece of 32 rows.
+        constexpr int TG = SA_EPI_GROUP;  // lanes per transpose group
+        constexpr int CW = 64 / TG;       // 32-bit words per chunk
+        uint32_t u[64];
 #pragma unroll
         for (int cc = 0; cc < 4; ++cc) {
           reg_fence32(o32[cc]);
 #pragma unroll
           for (int i = 0; i < 16; ++i)
-            w[cc][i] = pack_bf16(__uint_as_float(o32[cc][2 * i]) * inv, __uint_as_float(o32[cc][2 * i + 1]) * inv);
+            u[cc * 16 + i] =
+                pack_bf16(__uint_as_float(o32[cc][2 * i]) * inv, __uint_as_float(o32[cc][2 * i + 1]) * inv);
         }
-        const int j = lane & 3;
+        const int j = lane % TG;
 #pragma unroll
-        for (int b = 0; b < 2; ++b) {
-          const int m = 1 << b;
-          const bool jb = (j >> b) & 1;
+        for (int m = 1; m < TG; m <<= 1) {
+          const bool jb = (j & m) != 0;
 #pragma unroll
-          for (int c0 = 0; c0 < 4; ++c0) {
+          for (int c0 = 0; c0 < TG; ++c0) {
             if (c0 & m) continue;
             const int c1 = c0 | m;
 #pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              const uint32_t r = __shfl_xor_sync(FULL, jb ? w[c0][i] : w[c1][i], m);
+            for (int i = 0; i < CW; ++i) {
+              const uint32_t r = __shfl_xor_sync(FULL, jb ? u[c0 * CW + i] : u[c1 * CW + i], m);
               if (jb)
-                w[c0][i] = r;
+                u[c0 * CW + i] = r;
               else
-                w[c1][i] = r;
+                u[c1 * CW + i] = r;
             }
           }
         }
-        const int qd = lane >> 2;
+        // lane j of a group now holds, in slot k, chunk j (CW words) of the group's row k
+        const int gq = lane / TG;
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
-          const int r_local = c.q0 + wr * 32 + qd * 4 + kk;
+        for (int kk = 0; kk < TG; ++kk) {
+          const int r_local = c.q0 + wr * 32 + gq * TG + kk;
           if (r_local < p.T_q) {
             __nv_bfloat16* dst =
-                p.out + (int64_t)c.b * p.o_sb + (int64_t)c.h * p.o_sh + (int64_t)r_local * p.o_st + j * 32;
+                p.out + (int64_t)c.b * p.o_sb + (int64_t)c.h * p.o_sh + (int64_t)r_local * p.o_st + j * (2 * CW);
             if ((reinterpret_cast<uintptr_t>(dst) & 31u) == 0) {
-              st_global_v8(dst, w[kk]);
-              st_global_v8(dst + 16, w[kk] + 8);
+#pragma unroll
+              for (int v8 = 0; v8 < CW / 8; ++v8) st_global_v8(dst + 16 * v8, u + kk * CW + 8 * v8);
             } else {
               uint4* d4 = reinterpret_cast<uint4*>(dst);
 #pragma unroll
-              for (int i = 0; i < 4; ++i)
-                d4[i] = make_uint4(w[kk][4 * i], w[kk][4 * i + 1], w[kk][4 * i + 2], w[kk][4 * i + 3]);
+              for (int i = 0; i < CW / 4; ++i)
+                d4[i] = make_uint4(u[kk * CW + 4 * i], u[kk * CW + 4 * i + 1], u[kk * CW + 4 * i + 2],
+                                   u[kk * CW + 4 * i + 3]);
             }
           }
         }
