@@ -93,6 +93,19 @@ SA_API int sa_bigbird_pairs(const sa_bigbird_layout* layouts, int32_t n_groups, 
                      const int32_t* offsets, int32_t* pairs, int32_t max_pairs,
                      sa_stream_t stream);
 
+/* Decode rows (T_q = 1) of query heads [head_lo, head_lo + n_rows) for the key
+ * count *seq_len read on the device (the rows of sa_bigbird_offsets/_pairs with
+ * T_q = 1, T_k = *seq_len; BigBirdKeepRatioPattern's decode build,
+ * bigbird_pattern.py:533-583 with T_q = 1): offsets [n_rows, 2] = {0, nnz},
+ * pairs [n_rows, max_pairs] (row h holds its blocks, rest untouched). A row
+ * longer than max_pairs is cut and sets SA_DEV_ERR_INDEX in the device error
+ * word. A dense causal row is the layout (block_size, 0, window >= rows, 0).
+ * For graph-replayed decode, where the host does not see the growing length. */
+SA_API int sa_bigbird_decode_row(const sa_bigbird_layout* layouts, int32_t n_groups, int32_t n_heads,
+                                 int32_t head_lo, int32_t n_rows, const int32_t* seq_len, int32_t block_size,
+                                 int32_t variant, int32_t* offsets, int32_t* pairs, int32_t max_pairs,
+                                 sa_stream_t stream);
+
 /* Arbitrary retained-block masks. Replaces build_block_pairs_from_mask
  * (sparse_attentions/patterns/base.py:36-89).
  * sa_block_bitmap_from_token_mask: token mask [H, T_q, T_k] (bool/uint8,

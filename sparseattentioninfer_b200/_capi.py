@@ -19,6 +19,7 @@ EXPORTED = (
     "sa_device_error",
     "sa_bigbird_offsets",
     "sa_bigbird_pairs",
+    "sa_bigbird_decode_row",
     "sa_block_bitmap_from_token_mask",
     "sa_bitmap_offsets",
     "sa_bitmap_pairs",
@@ -120,6 +121,8 @@ def load(path: str | os.PathLike | None = None) -> ctypes.CDLL:
     lay = ctypes.POINTER(BigBirdLayout)
     lib.sa_bigbird_offsets.argtypes = [lay, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_p, _c_p]
     lib.sa_bigbird_pairs.argtypes = [lay, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_p, _c_p, _c_i32, _c_p]
+    lib.sa_bigbird_decode_row.argtypes = [lay, _c_i32, _c_i32, _c_i32, _c_i32, _c_p, _c_i32, _c_i32, _c_p, _c_p,
+                                          _c_i32, _c_p]
     lib.sa_block_bitmap_from_token_mask.argtypes = [_c_p, _c_i32, _c_i32, _c_i32, _c_i32, _c_p, _c_p]
     lib.sa_bitmap_offsets.argtypes = [_c_p, _c_i32, _c_i32, _c_i32, _c_p, _c_p]
     lib.sa_bitmap_pairs.argtypes = [_c_p, _c_i32, _c_i32, _c_i32, _c_p, _c_p, _c_i32, _c_p]

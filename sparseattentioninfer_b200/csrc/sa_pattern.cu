@@ -258,6 +258,35 @@ __global__ void token_mask_to_bitmap_kernel(const uint8_t* mask, int T_q, int T_
   }
 }
 
+// Decode rows (T_q = 1) of heads [head_lo, head_lo + n_rows) for the key count
+// in device memory: block rows depend on T_k only through nkb and the query
+// block (T_k - 1) / bs, so a CUDA graph replaying a growing cache can recompute
+// them on the device every step. offsets [n_rows, 2], pairs [n_rows, max_pairs].
+__global__ void bigbird_decode_row_kernel(BigBirdParams P, const int32_t* seq_len, int bs, int head_lo, int n_rows,
+                                          int32_t* offsets, int32_t* pairs, int max_pairs, int32_t* err) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n_rows) return;
+  const int T_k = max(1, __ldg(seq_len));
+  P.nqb = 1;
+  P.nkb = (T_k + bs - 1) / bs;
+  P.qb_off = (T_k - 1) / bs;
+  Range rr[4];
+  const int m = bigbird_row_ranges(P, head_lo + i, 0, rr);
+  int32_t* dst = pairs + (int64_t)i * max_pairs;
+  int pos = 0;
+  for (int k = 0; k < m; ++k)
+    for (int kb = rr[k].lo; kb < rr[k].hi; ++kb) {
+      if (pos < max_pairs) dst[pos] = kb;
+      ++pos;
+    }
+  if (pos > max_pairs) {
+    record_error(err, SA_DEV_ERR_INDEX);
+    pos = max_pairs;
+  }
+  offsets[2 * i] = 0;
+  offsets[2 * i + 1] = pos;
+}
+
 static int fill_bigbird(BigBirdParams* P, const sa_bigbird_layout* layouts, int n_groups, int n_heads, int T_q,
                         int T_k, int bs, int variant) {
   if (!layouts) return sa_fail(SA_ERR_INVALID, "layouts is NULL");
@@ -368,6 +397,23 @@ extern "C" int sa_kvlist_pairs(const int32_t* kv_block_list, int32_t H, int32_t 
   const int64_t rows = (int64_t)H * NQB;
   kvlist_pairs_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, s>>>(kv_block_list, H, NQB, max_kv, offsets, pairs,
                                                                  max_pairs);
+  SA_CHECK_CUDA(cudaGetLastError());
+  return SA_OK;
+}
+
+extern "C" int sa_bigbird_decode_row(const sa_bigbird_layout* layouts, int32_t n_groups, int32_t n_heads,
+                                     int32_t head_lo, int32_t n_rows, const int32_t* seq_len, int32_t block_size,
+                                     int32_t variant, int32_t* offsets, int32_t* pairs, int32_t max_pairs,
+                                     sa_stream_t stream) {
+  BigBirdParams P;
+  int rc = fill_bigbird(&P, layouts, n_groups, n_heads, 1, 1, block_size, variant);
+  if (rc) return rc;
+  if (variant == SA_BIGBIRD2) return sa_fail(SA_ERR_UNSUPPORTED, "decode rows: BigBird2 has no decode variant");
+  if (!seq_len || !offsets || !pairs || max_pairs <= 0) return sa_fail(SA_ERR_INVALID, "bad pointers / max_pairs");
+  if (head_lo < 0 || n_rows <= 0 || head_lo + n_rows > n_heads)
+    return sa_fail(SA_ERR_INVALID, "heads [%d, %d) outside [0, %d)", head_lo, head_lo + n_rows, n_heads);
+  bigbird_decode_row_kernel<<<(n_rows + 127) / 128, 128, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      P, seq_len, block_size, head_lo, n_rows, offsets, pairs, max_pairs, sa_device_error_ptr());
   SA_CHECK_CUDA(cudaGetLastError());
   return SA_OK;
 }

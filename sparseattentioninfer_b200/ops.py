@@ -83,6 +83,29 @@ def compile_bigbird(layouts: Sequence[Sequence[int]], n_heads: int, T_q: int, T_
     return pairs, offsets
 
 
+
+def bigbird_decode_row(layouts, n_heads: int, seq_len: torch.Tensor, block_size: int, pairs: torch.Tensor,
+                       offsets: torch.Tensor, *, head_lo: int = 0, variant: int = _capi.SA_BIGBIRD) -> None:
+    """Decode rows (T_q = 1) of query heads [head_lo, head_lo + pairs.shape[0]) for the
+    key count in ``seq_len`` (int32 device scalar), written into ``pairs``
+    [rows, W] and ``offsets`` [rows, 2] on the device (sa_bigbird_decode_row):
+    the rows compile_bigbird(layouts, n_heads, 1, T_k, ...) gives, without the
+    host knowing T_k (graph-replayed decode)."""
+    _require_cuda(seq_len, pairs, offsets)
+    if seq_len.dtype != torch.int32 or pairs.dtype != torch.int32 or offsets.dtype != torch.int32:
+        raise TypeError("int32 tensors expected")
+    rows = pairs.shape[0]
+    if offsets.shape != (rows, 2) or not pairs.is_contiguous() or not offsets.is_contiguous():
+        raise ValueError("pairs [rows, W] and offsets [rows, 2], contiguous")
+    lib = _capi.load()
+    n = len(layouts)
+    arr = (_capi.BigBirdLayout * n)(*[_capi.BigBirdLayout(*map(int, l)) for l in layouts])
+    with torch.cuda.device(pairs.device):
+        _capi.check(lib.sa_bigbird_decode_row(arr, n, n_heads, head_lo, rows, seq_len.data_ptr(), block_size, variant,
+                                              offsets.data_ptr(), pairs.data_ptr(), pairs.shape[1],
+                                              _stream(pairs.device)))
+
+
 def compile_block_bitmap(bitmap: torch.Tensor, *, width: int | None = None) -> tuple[torch.Tensor, torch.Tensor]:
     """Block bitmap [H, NQB, NKB] (nonzero = keep) -> CSR, as build_block_pairs_from_mask's
     CSR loop (patterns/base.py:75-89)."""

@@ -326,19 +326,12 @@ class Qwen3TPRunner:
         return (nxt, logits) if return_logits else nxt
 
     # -- graph-captured decode ---------------------------------------------------
-    def _refresh_graph_csr(self, T_k: int) -> None:
-        for dense, (gp, go) in self._g_csr.items():
-            pairs, offs = self.decode_csr(T_k, dense)
-            gp.zero_()
-            gp[:, : pairs.shape[1]].copy_(pairs)
-            go.copy_(offs)
-
     @torch.no_grad()
     def capture_decode(self) -> None:
         """Record one decode step (all layers, logits, argmax, position advance) in
         a CUDA graph. The step reads its position and key count from device
-        counters and its CSR from fixed buffers, which ``step_graph`` refreshes
-        when the step enters a new key block; everything else is replayed as is."""
+        counters and recomputes its decode CSR rows on the device from the key
+        count (ops.bigbird_decode_row), so replays need no host work."""
         if self.dense_impl == "sdpa" and len(self.sparse) < self.A.layers:
             raise RuntimeError("dense_impl='sdpa' cannot be captured (its length is a host value)")
         ops = self.ops
@@ -368,7 +361,12 @@ class Qwen3TPRunner:
                            workspace=ws, seq_len=self._g_len)
             return att.view(B, 1, -1)
 
+        dense_layout = [(self.bs, 0, 1 << 30, 0)]  # window wider than any cache: every causal block
+
         def body():
+            for dense, (gp, go) in self._g_csr.items():
+                ops.bigbird_decode_row(dense_layout if dense else [self.layout], A.heads, self._g_len, self.bs, gp, go,
+                                       head_lo=w.q_lo)
             logits = self._logits(self._forward(self._g_tok, 0, self._g_pos, attend))
             self._g_tok.copy_(logits.argmax(-1, keepdim=True))
             self._g_pos.add_(1)
@@ -383,7 +381,6 @@ class Qwen3TPRunner:
         # rewind the counters and record
         saved = self.length
         rewind(saved)
-        self._refresh_graph_csr(saved + 1)
         s = torch.cuda.Stream(device=dev)
         s.wait_stream(torch.cuda.current_stream(dev))
         with torch.cuda.stream(s):
@@ -411,8 +408,6 @@ class Qwen3TPRunner:
         if moved:
             self._g_pos.fill_(pos)
             self._g_len.fill_(pos + 1)
-        if pos % self.bs == 0 or moved:
-            self._refresh_graph_csr(pos + 1)
         if tok is not None:
             self._g_tok.copy_(tok)
         self._graph.replay()

@@ -97,3 +97,25 @@ def test_full_size_bigbird_against_oracle():
         rp, ro = op.bigbird_csr(layouts, H, T, T)
         np.testing.assert_array_equal(offs.cpu().numpy(), ro)
         np.testing.assert_array_equal(pairs.cpu().numpy(), rp)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("layouts,H,bs", [([(64, 2, 4, 2)], 32, 64), ([(128, 2, 4, 3)], 32, 128),
+                                          ([(64, 1, 2, 3), (64, 3, 5, 1)], 8, 64), ([(64, 0, 1 << 30, 0)], 4, 64)])
+def test_device_decode_rows_match_host_compiled_rows(layouts, H, bs):
+    """sa_bigbird_decode_row with the key count on the device gives the decode rows
+    compile_bigbird builds for T_q = 1, for lengths across block boundaries and
+    for a head sub-range (a tensor-parallel rank's rows)."""
+    from sparseattentioninfer_b200 import ops
+    width = 4096 // bs + 8 if layouts[0][2] >= (1 << 29) else max(g + w + r for _, g, w, r in layouts)
+    lo, n = (H // 2, H // 2)
+    for T_k in [1, bs - 1, bs, bs + 1, 3 * bs, 3 * bs + 7, 4000]:
+        sl = torch.tensor([T_k], dtype=torch.int32, device="cuda:0")
+        gp = torch.full((n, width), -7, dtype=torch.int32, device="cuda:0")
+        go = torch.zeros(n, 2, dtype=torch.int32, device="cuda:0")
+        ops.bigbird_decode_row(layouts, H, sl, bs, gp, go, head_lo=lo)
+        hp, ho = ops.compile_bigbird(layouts, H, 1, T_k, bs, device="cuda:0")
+        for i in range(n):
+            a, b = int(go[i, 1]), int(ho[lo + i, 1] - ho[lo + i, 0])
+            assert int(go[i, 0]) == 0 and a == b, (T_k, i)
+            assert torch.equal(gp[i, :a], hp[lo + i, int(ho[lo + i, 0]):int(ho[lo + i, 1])]), (T_k, i)
