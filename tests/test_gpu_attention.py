@@ -122,6 +122,23 @@ def test_prefill_strided_views():
     assert_close(out, ref, "strided")
 
 
+def test_prefill_output_rows_not_32_byte_aligned():
+    """Output rows 16 bytes apart from a 32-byte boundary on every other row (row
+    stride D + 8): the epilogue's 256-bit stores fall back to 16-byte stores there,
+    and the padding between rows is never written."""
+    B, Hq, Hkv, T, D, bs = 1, 4, 2, 384, 128, 128
+    q, k, v = sa.workloads.seeded_qkv(13, B, Hq, Hkv, T, T, D, dtype=torch.bfloat16)
+    bm = _random_csr(Hq, T, T, bs, 0.6, seed=6)
+    pairs, offs = op.csr_from_block_bitmap(bm)
+    ref = oracle.csr_attention(q.float(), k.float(), v.float(), pairs, offs, bs)
+    buf = torch.full((B, Hq, T, D + 8), 7.0, dtype=torch.bfloat16, device=DEV)
+    out = buf[..., :D]
+    ops.prefill_fwd(q.to(DEV), k.to(DEV), v.to(DEV), torch.from_numpy(pairs).to(DEV), torch.from_numpy(offs).to(DEV),
+                    bs, out=out)
+    assert_close(out, ref, "misaligned rows")
+    assert bool((buf[..., D:] == 7.0).all()), "padding between rows was written"
+
+
 DEC = [
     # B, Hq, Hkv, T_k, D, bs, density, n_split
     (4, 32, 8, 1000, 128, 64, 0.3, None),
