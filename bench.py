@@ -62,16 +62,26 @@ def load_peaks() -> tuple[dict, str]:
     return dict(FALLBACK_PEAKS), "fallback"
 
 
-def traffic_from_profile(name: str):
+def traffic_from_profile(name: str, **expect):
     """Per-launch DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) recorded
-    from an ncu capture in profiles/<name>; None when not captured yet."""
+    from an ncu capture in profiles/<name>; None when not captured yet, or when a
+    ``key: value`` line of the file differs from ``expect`` (the capture then
+    describes another launch shape than the one timed)."""
     p = ROOT / "profiles" / name
     if not p.exists():
         return None
+    fields = {}
     for line in p.read_text().splitlines():
-        if line.startswith("traffic_bytes_per_launch:"):
-            return float(line.split(":", 1)[1])
-    return None
+        if ":" in line and not line.startswith(" "):
+            key, val = line.split(":", 1)
+            fields[key.strip()] = val.strip()
+    for key, val in expect.items():
+        if fields.get(key) != str(val):
+            return None
+    try:
+        return float(fields["traffic_bytes_per_launch"])
+    except (KeyError, ValueError):
+        return None
 
 
 class ClockSampler:
@@ -126,6 +136,22 @@ class ClockSampler:
         os.unlink(self.path)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
                 "reasons": sorted(reasons), "samples": len(sm)}
+
+
+class L2Flush:
+    """Evicts the 126 MB L2 between timed launches: writes a 256 MiB buffer, then
+    reads another 256 MiB buffer so that the written lines leave L2 (written back)
+    before the timed kernel starts, instead of being written back while it runs."""
+
+    note = "L2 flushed before each step (256 MiB write, then 256 MiB read of another buffer)"
+
+    def __init__(self, device):
+        self.w = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+        self.r = torch.ones(64 << 20, dtype=torch.float32, device=device)
+
+    def __call__(self):
+        self.w.zero_()
+        self.r.sum()
 
 
 def dist_env():
@@ -201,11 +227,17 @@ def run_reference(args) -> None:
     emit(line)
 
 
-def time_decode(device) -> dict:
-    """Split-KV decode on the Qwen3-4B-shaped attention layer: B=32, Hq=32,
+def time_decode(device, layers: int = 8) -> dict:
+    """Block-sparse decode on the Qwen3-4B-shaped attention layer: B=32, Hq=32,
     Hkv=8, D=128, T_k=32768 bf16 cache, BigBird (64, 2, 4, 2). Algorithmic bytes
     = union of retained KV blocks per (b, kv-group) x 64 x 128 x 2 (K,V) x 2 B
-    + q/out."""
+    + q/out.
+
+    Two timings, L2 flushed before each (bench.L2Flush):
+      single      one launch, CUDA events around it (includes the launch latency);
+      per_layer   `layers` layers decoded back to back in one CUDA graph, each
+                  layer with its own KV cache (as the model's sparse layers are),
+                  graph time / layers — the kernel's steady state."""
     from sparseattentioninfer_b200 import BigBirdKeepRatioPattern, ops, workloads as wl
     Bd, Hq, Hkv, T = 32, 32, 8, 32768
     q, k, v = wl.seeded_qkv(7, Bd, Hq, Hkv, 1, T, D, device=device, dtype=torch.bfloat16)
@@ -221,29 +253,57 @@ def time_decode(device) -> dict:
         u = set().union(*rows[gi * 4:(gi + 1) * 4])
         nblk += sum(1 for kb in u if kb * 64 < T)
     alg_bytes = Bd * nblk * 64 * D * 2 * 2 + 2 * Bd * Hq * D * 2
+    caches = [(k, v)] + [tuple(torch.randn(Bd, Hkv, T, D, device=device, dtype=torch.bfloat16) for _ in range(2))
+                         for _ in range(layers - 1)]
     ns = ops.default_n_split(q, k)
     ws = (torch.empty(Bd * Hq * ns * D, device=device), torch.empty(Bd * Hq * ns * 2, device=device))
     out = torch.empty_like(q)
-    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=device)
-    for _ in range(5):
-        ops.decode_fwd(q, k, v, pairs, offs, 64, n_split=ns, out=out, workspace=ws)
-    # Each timed launch follows a 256 MB L2 flush on the same stream; iterations
-    # are enqueued back to back (one synchronize at the end), so the host-side
-    # launch work of a step overlaps the previous flush and the events measure
-    # device time, as in a graph replay.
+    flush = L2Flush(device)
+
+    def launch(li):
+        kc, vc = caches[li]
+        ops.decode_fwd(q, kc, vc, pairs, offs, 64, n_split=ns, out=out, workspace=ws)
+
+    for li in range(layers):
+        launch(li)
+    # single launches: enqueued back to back (one synchronize at the end), so
+    # the host-side work of a step overlaps the previous flush
     evs = []
-    for _ in range(30):
-        flush.zero_()
+    for i in range(30):
+        flush()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
-        ops.decode_fwd(q, k, v, pairs, offs, 64, n_split=ns, out=out, workspace=ws)
+        launch(i % layers)
         e1.record()
         evs.append((e0, e1))
     torch.cuda.synchronize()
-    t = statistics.median(a.elapsed_time(b) / 1e3 for a, b in evs)
-    return {"workload": "qwen3_4b_layer_decode_b32_h32kv8_t32768_bigbird64_2_4_2", "us_per_step": t * 1e6,
-            "alg_bytes": alg_bytes, "achieved_gbs": alg_bytes / t / 1e9, "n_split": ns,
-            "note": f"{1 if ns == 1 else 2} launch(es) per step; L2 flushed before each step; device time"}
+    t_single = statistics.median(a.elapsed_time(b) / 1e3 for a, b in evs)
+    # all layers in one graph
+    g = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream(device)
+    s.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(g, stream=s):
+            for li in range(layers):
+                launch(li)
+    torch.cuda.current_stream(device).wait_stream(s)
+    evs = []
+    for _ in range(10):
+        flush()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        g.replay()
+        e1.record()
+        evs.append((e0, e1))
+    torch.cuda.synchronize()
+    t_layer = statistics.median(a.elapsed_time(b) / 1e3 for a, b in evs) / layers
+    del g, caches
+    return {"workload": "qwen3_4b_layer_decode_b32_h32kv8_t32768_bigbird64_2_4_2",
+            "us_per_layer": t_layer * 1e6, "us_single_launch": t_single * 1e6,
+            "alg_bytes": alg_bytes, "achieved_gbs": alg_bytes / t_layer / 1e9,
+            "achieved_gbs_single_launch": alg_bytes / t_single / 1e9, "n_split": ns,
+            "note": f"{1 if ns == 1 else 2} launch(es) per layer; per_layer = {layers} layers (own KV caches) "
+                    f"back to back in one CUDA graph / {layers}; " + flush.note}
 
 
 def time_gqa_layer(device, rank: int, world: int) -> dict:
@@ -607,7 +667,8 @@ def run_ours(args) -> None:
         hb = float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))
         line["decode"]["roofline_frac"] = line["decode"]["achieved_gbs"] / hb
         line["decode"]["peak_gbs"] = hb
-        line["decode"]["traffic"] = traffic_from_profile("decode_qwen3_4b_layer_ncu.txt")
+        line["decode"]["traffic"] = traffic_from_profile("decode_qwen3_4b_layer_ncu.txt",
+                                                         n_split=line["decode"]["n_split"])
     except Exception as e:  # noqa: BLE001
         line["decode"] = {"error": repr(e)}
     line["gqa_layer"] = gqa

@@ -179,7 +179,10 @@ SA_API int sa_prefill_fwd(const sa_attn_args* args, sa_stream_t stream);
  * random blocks differ per query head, bigbird_pattern.py:23-41).
  * Scratch (caller-allocated, float32): partial_o [B, Hq, n_split, D] and
  * partial_ml [B, Hq, n_split, 2]; a second kernel merges the splits into out.
- * n_split in [1, 64]; Hq/Hkv <= 8; D in {64, 128}.
+ * n_split in [1, 64]; Hq/Hkv in {1, 2, 4, 8}; D in {64, 128};
+ * ceil(T_k / block_size) <= 8192 and min(ceil(T_k / block_size),
+ * (Hq/Hkv) * pairs_stride) <= 2048 (the union of a KV group's rows is built in
+ * shared memory), SA_ERR_UNSUPPORTED otherwise.
  * ------------------------------------------------------------------------- */
 SA_API int sa_decode_fwd(const sa_attn_args* args, int32_t n_split, float* partial_o,
                   float* partial_ml, sa_stream_t stream);
@@ -197,8 +200,13 @@ SA_API int sa_decode_fwd(const sa_attn_args* args, int32_t n_split, float* parti
  * before any stream capture. All calls share the one array: calls that overlap
  * on the GPU (other streams, other threads) race and must be serialised by the
  * caller. Every split result is fully rewritten by each call, so nothing has to
- * start at zero. Same arguments, output and limits as sa_decode_fwd otherwise.
+ * start at zero. With n_split == 1 the kernel writes the output directly and
+ * the array is not used (no size limit). Same arguments, output, limits and
+ * error codes as sa_decode_fwd otherwise.
  * ------------------------------------------------------------------------- */
+#define SA_DECODE_SCRATCH_FLOATS (4 * 1024 * 1024)
+SA_API int sa_decode_fwd_noalloc(const sa_attn_args* args, int32_t n_split, sa_stream_t stream);
+
 /* ---------------------------------------------------------------------------
  * sa_decode_fwd with the key count read from device memory: args->k / args->v
  * span args->T_k rows (the cache capacity) and the kernel attends to keys
@@ -316,9 +324,6 @@ SA_API int sa_ar_ipc_close(void* ptr);
 SA_API int sa_allreduce_add_rms_norm(const sa_ar_peers* peers, int64_t data_offset, void* x, const void* weight,
                                      void* out, int64_t rows, int32_t n, int64_t x_stride, int64_t out_stride,
                                      float eps, sa_stream_t stream);
-
-#define SA_DECODE_SCRATCH_FLOATS (4 * 1024 * 1024)
-SA_API int sa_decode_fwd_noalloc(const sa_attn_args* args, int32_t n_split, sa_stream_t stream);
 
 #ifdef __cplusplus
 }

@@ -406,9 +406,8 @@ using namespace sa;
 
 int sa_validate_attn_args(const sa_attn_args* a, bool decode);
 
-// Fills DecodeParams from the C ABI arguments (shared with the no-scratch variant).
-int sa_decode_prepare(const sa_attn_args* a, int32_t n_split, float* partial_o, float* partial_ml,
-                      DecodeParams* prm) {
+// Host-side checks shared by every decode entry point (before any CUDA call).
+static int decode_check(const sa_attn_args* a, int32_t n_split) {
   int rc = sa_validate_attn_args(a, true);
   if (rc) return rc;
   if (a->T_q != 1) return sa_fail(SA_ERR_INVALID, "decode needs T_q == 1 (got %d)", a->T_q);
@@ -416,6 +415,27 @@ int sa_decode_prepare(const sa_attn_args* a, int32_t n_split, float* partial_o, 
   if (G != 1 && G != 2 && G != 4 && G != 8)
     return sa_fail(SA_ERR_UNSUPPORTED, "Hq/Hkv = %d unsupported for decode (1, 2, 4 or 8)", G);
   if (n_split < 1 || n_split > 64) return sa_fail(SA_ERR_INVALID, "n_split %d not in [1, 64]", n_split);
+  // Shared-memory limits of one CTA: the membership words cover NKB <= 8192 key
+  // blocks and the union list holds kMaxUnion blocks; the union of a group's G
+  // rows has at most min(NKB, G * pairs_stride) blocks.
+  const int64_t nkb = ((int64_t)a->T_k + a->block_size - 1) / a->block_size;
+  if (nkb > (int64_t)kMaxNkbWords * 4)
+    return sa_fail(SA_ERR_UNSUPPORTED, "decode supports ceil(T_k / block_size) <= %d (got %lld)", kMaxNkbWords * 4,
+                   (long long)nkb);
+  const int64_t ub = nkb < (int64_t)G * a->pairs_stride ? nkb : (int64_t)G * a->pairs_stride;
+  if (ub > kMaxUnion)
+    return sa_fail(SA_ERR_UNSUPPORTED,
+                   "decode unions up to %d blocks per KV group; min(ceil(T_k / block_size), (Hq/Hkv) * "
+                   "pairs_stride) = %lld",
+                   kMaxUnion, (long long)ub);
+  return SA_OK;
+}
+
+// Fills DecodeParams from the C ABI arguments (shared with the no-scratch variant).
+int sa_decode_prepare(const sa_attn_args* a, int32_t n_split, float* partial_o, float* partial_ml,
+                      DecodeParams* prm) {
+  int rc = decode_check(a, n_split);
+  if (rc) return rc;
   if (!partial_o || !partial_ml) return sa_fail(SA_ERR_INVALID, "NULL scratch pointer");
   memset(prm, 0, sizeof(*prm));
   prm->chk = a->block_size < kDecChunk ? a->block_size : kDecChunk;
@@ -499,22 +519,22 @@ static int decode_scratch_ptr(float** out) {
 }
 
 extern "C" int sa_decode_fwd_noalloc(const sa_attn_args* a, int32_t n_split, sa_stream_t stream) {
-  if (!a) return sa_fail(SA_ERR_INVALID, "args is NULL");
-  if (n_split < 1 || n_split > 64) return sa_fail(SA_ERR_INVALID, "n_split %d not in [1, 64]", n_split);
-  if (a->B <= 0 || a->Hq <= 0 || (a->D != 64 && a->D != 128))
-    return sa_fail(SA_ERR_INVALID, "bad B/Hq/D (B=%d Hq=%d D=%d)", a->B, a->Hq, a->D);
+  int rc = decode_check(a, n_split);  // same checks and error codes as sa_decode_fwd
+  if (rc) return rc;
+  // With one split the kernel writes the output directly and never touches the
+  // scratch array, so only n_split > 1 is bounded by its size.
   const int64_t rows = (int64_t)a->B * a->Hq * n_split;
   const int64_t need = rows * (a->D + 2);
-  if (need > (int64_t)SA_DECODE_SCRATCH_FLOATS)
+  if (n_split > 1 && need > (int64_t)SA_DECODE_SCRATCH_FLOATS)
     return sa_fail(SA_ERR_INVALID,
                    "decode scratch needs %lld floats (B*Hq*n_split*(D+2)), the built-in array holds %d; "
                    "lower n_split or use sa_decode_fwd with caller scratch",
                    (long long)need, (int)SA_DECODE_SCRATCH_FLOATS);
   float* base = nullptr;
-  int rc = decode_scratch_ptr(&base);
-  if (rc) return rc;
+  if ((rc = decode_scratch_ptr(&base))) return rc;
   DecodeParams prm;
-  rc = sa_decode_prepare(a, n_split, base, base + rows * a->D, &prm);
+  // n_split == 1: the partial pointers are unused; point both at the array start.
+  rc = sa_decode_prepare(a, n_split, base, n_split > 1 ? base + rows * a->D : base, &prm);
   if (rc) return rc;
   return sa_decode_launch(prm, a, reinterpret_cast<cudaStream_t>(stream));
 }

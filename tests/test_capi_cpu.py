@@ -72,6 +72,21 @@ def test_decode_host_validation():
     assert lib.sa_decode_fwd(ctypes.byref(a), 2, 1, 1, None) == _capi.SA_ERR_INVALID  # T_q != 1
     a = _args(T_q=1, Hq=48, Hkv=4)
     assert lib.sa_decode_fwd(ctypes.byref(a), 2, 1, 1, None) == _capi.SA_ERR_UNSUPPORTED  # group 12
+    a = _args(T_q=1, T_k=64 * 8193, block_size=64)
+    assert lib.sa_decode_fwd(ctypes.byref(a), 1, 1, 1, None) == _capi.SA_ERR_UNSUPPORTED  # NKB > 8192
+    assert b"8192" in lib.sa_last_error()
+    a = _args(T_q=1, T_k=64 * 4096, block_size=64, pairs_stride=4096)
+    assert lib.sa_decode_fwd(ctypes.byref(a), 1, 1, 1, None) == _capi.SA_ERR_UNSUPPORTED  # union > 2048
+    assert b"2048" in lib.sa_last_error()
+
+
+def test_noalloc_host_validation_matches_decode():
+    """The allocation-free entry point returns the same error codes as sa_decode_fwd."""
+    lib = _capi.load()
+    for kw in ({"D": 96}, {"T_q": 2}, {"B": 0}):
+        a = _args(**{"T_q": 1, **kw})
+        assert lib.sa_decode_fwd_noalloc(ctypes.byref(a), 1, None) == lib.sa_decode_fwd(ctypes.byref(a), 1, 1, 1,
+                                                                                         None)
 
 
 def test_pattern_host_validation():

@@ -140,12 +140,14 @@ def test_prefill_output_rows_not_32_byte_aligned():
 
 
 DEC = [
-    # B, Hq, Hkv, T_k, D, bs, density, n_split
+    # B, Hq, Hkv, T_k, D, bs, density, n_split (None = default)
     (4, 32, 8, 1000, 128, 64, 0.3, None),
     (2, 8, 8, 777, 64, 64, 0.5, 3),
     (3, 16, 2, 2048, 128, 128, 0.2, 7),
     (2, 8, 4, 64, 128, 64, 1.0, 2),
     (1, 8, 1, 4099, 128, 16, 0.1, None),
+    (2, 16, 4, 3000, 128, 256, 0.4, 5),     # 256-key blocks: four stages per block
+    (5, 24, 3, 2500, 64, 32, 0.25, 11),
 ]
 
 
@@ -159,6 +161,38 @@ def test_decode_vs_oracle(case):
     out = ops.decode_fwd(q.to(DEV), k.to(DEV), v.to(DEV), torch.from_numpy(pairs).to(DEV),
                          torch.from_numpy(offs).to(DEV), bs, n_split=ns)
     assert_close(out, ref, str(case))
+    assert _capi.device_error() == 0
+
+
+def test_decode_empty_groups_and_rows():
+    """KV groups whose rows are all empty give zero rows; a head with an empty
+    row inside a non-empty group gives zeros too (reference: l == 0 -> 0,
+    universal_sparse_attn.py:152)."""
+    B, Hq, Hkv, T_k, D, bs = 3, 16, 4, 900, 128, 64
+    q, k, v = sa.workloads.seeded_qkv(5, B, Hq, Hkv, 1, T_k, D, dtype=torch.bfloat16)
+    bm = _random_csr(Hq, 1, T_k, bs, 0.5, seed=3)
+    bm[0:4] = 0      # group 0: no head keeps a block
+    bm[9] = 0        # group 2: head 9 keeps nothing, its neighbours do
+    pairs, offs = op.csr_from_block_bitmap(bm)
+    ref = oracle.csr_attention(q.float(), k.float(), v.float(), pairs, offs, bs)
+    for ns in (1, 3):
+        out = ops.decode_fwd(q.to(DEV), k.to(DEV), v.to(DEV), torch.from_numpy(pairs).to(DEV),
+                             torch.from_numpy(offs).to(DEV), bs, n_split=ns)
+        assert_close(out, ref, f"n_split={ns}")
+        assert bool((out[:, 0:4] == 0).all()) and bool((out[:, 9] == 0).all())
+    assert _capi.device_error() == 0
+
+
+def test_decode_seqlen_matches_host_length():
+    """Live key count from device memory over a longer cache == host length on a slice."""
+    B, Hq, Hkv, cap, D, bs = 2, 32, 8, 4096, 128, 64
+    q, k, v = sa.workloads.seeded_qkv(6, B, Hq, Hkv, 1, cap, D, device=DEV, dtype=torch.bfloat16)
+    for T_k in (1, 63, 64, 65, 2000, 4096):
+        pairs, offs = ops.compile_bigbird([(64, 2, 4, 2)], Hq, 1, T_k, bs, device=DEV)
+        ref = ops.decode_fwd(q, k[:, :, :T_k], v[:, :, :T_k], pairs, offs, bs)
+        sl = torch.tensor([T_k], dtype=torch.int32, device=DEV)
+        got = ops.decode_fwd(q, k, v, pairs, offs, bs, seq_len=sl)
+        assert torch.equal(got, ref), T_k
     assert _capi.device_error() == 0
 
 

@@ -45,6 +45,7 @@ def test_noalloc_matches_caller_scratch_twice():
         # seed, B, Hq, Hkv, T_k, D, layouts, n_split
         (1, 4, 32, 8, 3000, 128, [(64, 2, 4, 2)], 3),
         (2, 2, 8, 8, 777, 64, [(64, 1, 3, 1)], 5),
+        (4, 3, 16, 4, 1500, 128, [(64, 2, 4, 2)], 1),   # one split: output written directly
     ]
     for seed, B, Hq, Hkv, T_k, D, layouts, ns in cases:
         q, k, v, pairs, offs = _decode_case(seed, B, Hq, Hkv, T_k, D, layouts)
@@ -71,3 +72,19 @@ def test_noalloc_rejects_requests_beyond_the_array():
     with pytest.raises(_capi.SaError, match="decode scratch needs"):
         _call_noalloc(q, k, v, pairs, offs, 64, n_split)
     assert math.isfinite(float(q.float().sum()))
+
+
+@pytest.mark.gpu
+def test_noalloc_one_split_has_no_size_limit():
+    """With n_split == 1 the array is not used, so shapes beyond it still run."""
+    B, Hq, Hkv, T_k, D = 256, 64, 8, 1024, 128
+    q, k, v, pairs, offs = _decode_case(5, 1, Hq, Hkv, T_k, D, [(64, 2, 4, 2)])
+    q = q.expand(B, -1, -1, -1).contiguous()
+    k = k.expand(B, -1, -1, -1).contiguous()
+    v = v.expand(B, -1, -1, -1).contiguous()
+    assert B * Hq * 2 * (D + 2) > 4 * 1024 * 1024  # n_split = 2 would not fit
+    ref = ops.decode_fwd(q, k, v, pairs, offs, 64, n_split=1)
+    got = _call_noalloc(q, k, v, pairs, offs, 64, 1)
+    torch.cuda.synchronize()
+    assert torch.equal(got, ref)
+    assert _capi.device_error() == 0
