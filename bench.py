@@ -6,11 +6,12 @@ Headline (one JSON line on rank 0): "sparse-attn prefill TFLOP/s on retained
 blocks" on the arbitrary block-mask prefill configuration (B=4, H=32, S=8192,
 D=128, bf16, block 128, causal blocks kept with p=0.25, diagonal always) —
 FLOPs counted as 4*bs^2*D per retained (b, head, q-block, k-block) entry.
-A step is one prefill over the whole batch. With N GPUs each rank processes
-its own 32-head shard (heads sharded by KV group, no collective: weak scaling).
+A step is one prefill over the whole batch. With N GPUs the 32 heads are split
+across the ranks (rank r owns heads [32r/N, 32(r+1)/N), no collective): strong
+scaling of one fixed layer.
 
-Extra keys: roofline of the prefill kernel (vs the measured dense bf16 peak,
-burst and sustained), e2e (same metric through the public backend API with
+Extra keys: roofline of the prefill kernel (vs the measured dense bf16 burst
+peak), e2e (same metric through the public backend API with
 pinned host buffers and the H2D/D2H copies in the timed region), cpu_baseline
 (the CPU restatement of the reference's masked-dense algorithm on a bounded
 sample), decode (the split-KV decode kernel on the Qwen3-4B-shaped layer, HBM
@@ -161,17 +162,48 @@ def dist_env():
     return world, rank, local
 
 
-def make_workload(rank: int, device):
-    """Config-2 shard of this rank: q/k/v N(0,1) bf16 (seed 1000+rank) and the
-    Bernoulli block bitmap (seed rank), CSR compiled on the device."""
+def load_workloads():
+    """sparseattentioninfer_b200/workloads.py (plain torch: seeded inputs and
+    patterns) loaded by path, so that the reference arm never imports the package
+    (importing it loads the CUDA library)."""
+    import importlib.util
+    if "_sa_workloads" in sys.modules:
+        return sys.modules["_sa_workloads"]
+    spec = importlib.util.spec_from_file_location("_sa_workloads", ROOT / "sparseattentioninfer_b200" / "workloads.py")
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules["_sa_workloads"] = mod  # dataclasses look their module up here
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def global_bitmap():
+    """The config-2 Bernoulli block bitmap of the whole layer [H, 64, 64] (CPU generator, seed 0):
+    the same on every rank and in both arms."""
+    return load_workloads().bernoulli_block_bitmap(H, S // BS, S // BS, P_KEEP, seed=0)
+
+
+def head_range(rank: int, world: int) -> tuple[int, int]:
+    """Config 2 is strong-scaled: rank r of N owns query heads [r*H/N, (r+1)*H/N)."""
+    if H % world:
+        raise ValueError(f"--gpus {world} must divide the {H} heads")
+    return rank * H // world, (rank + 1) * H // world
+
+
+def make_workload(rank: int, world: int, device):
+    """This rank's shard of config 2: its heads of the global bitmap, q/k/v N(0,1)
+    bf16 drawn on the device (seed 1000+rank; values do not change the work), CSR
+    compiled on the device."""
     from sparseattentioninfer_b200 import BlockMaskPattern, workloads as wl
-    q, k, v = wl.seeded_qkv(1000 + rank, B, H, H, S, S, D, device=device, dtype=torch.bfloat16)
-    nb = S // BS
-    bitmap = wl.bernoulli_block_bitmap(H, nb, nb, P_KEEP, seed=rank, device=device)
+    h0, h1 = head_range(rank, world)
+    q, k, v = wl.seeded_qkv(1000 + rank, B, h1 - h0, h1 - h0, S, S, D, device=device, dtype=torch.bfloat16)
+    bitmap = global_bitmap()[h0:h1].contiguous().to(device)
     md = BlockMaskPattern(bitmap, BS).build(q, k)
     nnz = int(md.block_pair_offsets[:, -1].long().sum().item())
     flops = 4 * BS * BS * D * nnz * B
     return q, k, v, md, bitmap, flops
+
+
+REF_SLICES = ((0, 0), (0, 1))  # (b, h) slices of config 2 timed by every reference step
 
 
 def cpu_sample(bitmap_cpu: torch.Tensor, seconds: float, max_slices: int, threads: int):
@@ -179,14 +211,14 @@ def cpu_sample(bitmap_cpu: torch.Tensor, seconds: float, max_slices: int, thread
     (b, h) slices of the workload until `seconds` elapsed; returns
     (TFLOP/s on retained blocks, slices done, wall seconds)."""
     import oracle
-    from sparseattentioninfer_b200 import workloads as wl
+    wl = load_workloads()
     torch.set_num_threads(threads)
-    q, k, v = wl.seeded_qkv(1000, 1, 1, 1, S, S, D, dtype=torch.bfloat16)
-    q, k, v = q.float(), k.float(), v.float()
     flops = done = 0
     t0 = time.perf_counter()
-    for h in range(max_slices):
-        hh = h % H
+    for i in range(max_slices):
+        hh = i % H
+        q, k, v = wl.seeded_qkv(1000 + hh, 1, 1, 1, S, S, D, dtype=torch.bfloat16)
+        q, k, v = q.float(), k.float(), v.float()
         bm = bitmap_cpu[hh].bool()
         keep_fn = (lambda _h, r0, r1, bm=bm: bm[torch.arange(r0, r1) // BS][:, torch.arange(S) // BS])
         oracle.masked_sdpa_chunked(q, k, v, keep_fn, row_chunk=1024)
@@ -199,29 +231,44 @@ def cpu_sample(bitmap_cpu: torch.Tensor, seconds: float, max_slices: int, thread
 
 
 def run_reference(args) -> None:
+    """The reference's own algorithm for this path (MaskedSdpaBackend, restated in
+    oracle/; the reference is pure Python) on the host cores. Every step times
+    the same fixed (b, h) slices of config 2 (REF_SLICES) and reports retained-
+    block TFLOP/s over them — the rate a full step would run at, since every
+    (b, h) slice is the same masked-dense computation over its own block mask.
+    Nothing here imports the CUDA package."""
     world, rank, _ = dist_env()
     if rank != 0:
         return
-    from sparseattentioninfer_b200 import workloads as wl
+    import oracle
+    wl = load_workloads()
     threads = os.cpu_count() or 1
-    nb = S // BS
-    bitmap = wl.bernoulli_block_bitmap(H, nb, nb, P_KEEP, seed=0)
-    per_step_slices = 2
-    times, rates = [], []
+    torch.set_num_threads(threads)
+    bitmap = global_bitmap()
+    sl = []
+    for b, h in REF_SLICES:
+        q, k, v = wl.seeded_qkv(1000 + h, 1, 1, 1, S, S, D, dtype=torch.bfloat16)
+        bm = bitmap[h].bool()
+        sl.append((q.float(), k.float(), v.float(), bm, 4 * BS * BS * D * int(bm.sum())))
+    flops = sum(x[4] for x in sl)
+    times = []
     for i in range(args.warmup + args.steps):
-        rate, done, wall = cpu_sample(bitmap, 1e9, per_step_slices, threads)
+        t0 = time.perf_counter()
+        for q, k, v, bm, _ in sl:
+            keep_fn = (lambda _h, r0, r1, bm=bm: bm[torch.arange(r0, r1) // BS][:, torch.arange(S) // BS])
+            oracle.masked_sdpa_chunked(q, k, v, keep_fn, row_chunk=1024)
         if i >= args.warmup:
-            times.append(wall)
-            rates.append(rate)
-    value = statistics.mean(rates)
+            times.append(time.perf_counter() - t0)
+    value = flops / statistics.mean(times) / 1e12
+    sample = (f"(b, h) slices {list(REF_SLICES)} of B={B},H={H},S={S},D={D} per step, masked-dense fp32; "
+              f"value = their retained-block FLOPs / their wall time")
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * statistics.mean(times),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "arbitrary_block_mask_b4_h32_s8192_d128_bs128_p0.25",
-                   "sample": f"{per_step_slices} (b,h) slices per step of the B=4,H=32 workload"},
-        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads, "kind": "port",
-                         "sample": f"{per_step_slices} (b,h) slices of S=8192 per step, masked-dense fp32"},
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "arbitrary_block_mask_b4_h32_s8192_d128_bs128_p0.25", "sample": sample,
+                   "extrapolation": "a full step is 128 such slices: step time = 64 x the sampled time"},
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     emit(line)
@@ -306,24 +353,40 @@ def time_decode(device, layers: int = 8) -> dict:
                     f"back to back in one CUDA graph / {layers}; " + flush.note}
 
 
+def lpt_assign(loads, world: int) -> list[list[int]]:
+    """Longest-processing-time assignment of units (by load, heaviest first) to the
+    least-loaded rank; ties by lower index. Deterministic on every rank."""
+    order = sorted(range(len(loads)), key=lambda i: (-loads[i], i))
+    bins, tot = [[] for _ in range(world)], [0] * world
+    for i in order:
+        r = min(range(world), key=lambda j: (tot[j], j))
+        bins[r].append(i)
+        tot[r] += loads[i]
+    return [sorted(b) for b in bins]
+
+
 def time_gqa_layer(device, rank: int, world: int) -> dict:
     """Config 3: GQA layer with Qwen3-4B shapes, B=2, Hq=32, Hkv=8, D=128,
     S=16384 bf16; q and k get per-head RMSNorm (unit weight) and RoPE (theta 1e6);
     per-KV-group BigBird layouts (block 64) drawn from seed 2 (workloads.config3_group_layouts).
-    With N ranks, rank r owns KV groups [r*8/N, (r+1)*8/N) and their query heads."""
+    Sharded by KV group: the 8 groups are assigned to the N ranks by retained-block
+    count (LPT), each rank holds its groups' K/V and query heads."""
     from sparseattentioninfer_b200 import ops, workloads as wl
     B3, Hq, Hkv, S3, D3 = 2, 32, 8, 16384, 128
+    G3 = Hq // Hkv
     layouts = wl.config3_group_layouts()
-    gpr = max(1, Hkv // world)  # KV groups per rank
-    g0 = (rank * gpr) % Hkv
-    hq = gpr * (Hq // Hkv)
-    q, k, v = wl.seeded_qkv(30 + rank, B3, hq, gpr, S3, S3, D3, device=device, dtype=torch.bfloat16)
-    q, k = wl.rope(wl.rms_norm(q)), wl.rope(wl.rms_norm(k))
     # the reference indexes random blocks by the global query-head index: compile the
     # full layer's CSR and keep this rank's rows, so every shard matches the whole layer
-    pairs, offs = ops.compile_bigbird(layouts, Hq, S3, S3, 64, device=device)
-    h_lo = g0 * (Hq // Hkv)
-    pairs, offs = pairs[h_lo:h_lo + hq].contiguous(), offs[h_lo:h_lo + hq].contiguous()
+    pairs_all, offs_all = ops.compile_bigbird(layouts, Hq, S3, S3, 64, device=device)
+    head_nnz = offs_all[:, -1].long().cpu().tolist()
+    group_nnz = [sum(head_nnz[g * G3:(g + 1) * G3]) for g in range(Hkv)]
+    groups = lpt_assign(group_nnz, world)[rank % world] if world <= Hkv else [rank % Hkv]
+    heads = [g * G3 + j for g in groups for j in range(G3)]
+    hq, gpr = len(heads), len(groups)
+    q, k, v = wl.seeded_qkv(30 + rank, B3, hq, gpr, S3, S3, D3, device=device, dtype=torch.bfloat16)
+    q, k = wl.rope(wl.rms_norm(q)), wl.rope(wl.rms_norm(k))
+    idx = torch.tensor(heads, device=device)
+    pairs, offs = pairs_all.index_select(0, idx).contiguous(), offs_all.index_select(0, idx).contiguous()
     nnz = int(offs[:, -1].long().sum().item())
     flops = 4 * 64 * 64 * D3 * nnz * B3
     out = torch.empty_like(q)
@@ -339,6 +402,7 @@ def time_gqa_layer(device, rank: int, world: int) -> dict:
         ts.append(e0.elapsed_time(e1) / 1e3)
     t = statistics.median(ts)
     return {"workload": "gqa_qwen3_4b_b2_h32kv8_s16384_d128_bigbird64_groups_seed2", "kv_groups_per_rank": gpr,
+            "groups": groups, "assignment": "KV groups to ranks by retained blocks (LPT)",
             "layouts": [list(x) for x in layouts], "retained_blocks": nnz * B3, "ms": t * 1e3,
             "tflops": flops / t / 1e12, "flops": flops}
 
@@ -516,7 +580,7 @@ def run_ours(args) -> None:
     from sparseattentioninfer_b200 import ops
 
     peaks, peak_kind = load_peaks()
-    q, k, v, md, bitmap, flops = make_workload(rank, device)
+    q, k, v, md, bitmap, flops = make_workload(rank, world, device)
     pairs, offs = md.block_pairs, md.block_pair_offsets
     out = torch.empty_like(q)
     stream = torch.cuda.current_stream(device)
@@ -640,20 +704,16 @@ def run_ours(args) -> None:
     line = {
         "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": elapsed / args.steps * 1e3, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
         "config": {"workload": "arbitrary_block_mask_b4_h32_s8192_d128_bs128_p0.25",
-                   "per_rank": f"B={B} H={H} S={S} D={D} (rank r owns heads [32r, 32r+32))",
+                   "per_rank": f"B={B} H={H // world} of {H} S={S} D={D} (rank r owns heads [r*{H}/N, (r+1)*{H}/N); "
+                               "no collective)",
                    "retained_blocks_per_rank": flops // (4 * BS * BS * D * B),
                    "l2": "inputs 805 MB per rank > 126 MB L2; no flush"},
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                      "frac": achieved / peak, "peak_kind": f"{peak_kind} bf16 dense (burst)",
                      "traffic": traffic_from_profile("prefill_cfg2_ncu.txt"),
-                     "kernel": "sa::prefill_kernel<128,64,2>", "traffic_note": "ncu dram read+write of one launch, profiles/prefill_cfg2_ncu.txt", "launch_ms": t_launch * 1e3,
-                     "sustained": {"achieved": value / max(1, world),
-                                   "peak": float(peaks.get("bf16_tflops_sustained", 1400.0)),
-                                   "frac": value / max(1, world) / float(peaks.get("bf16_tflops_sustained", 1400.0)),
-                                   "note": "per-GPU throughput of the K back-to-back steps against the "
-                                           "sustained (power-capped) cuBLAS figure"}},
+                     "kernel": "sa::prefill_kernel<128,64,2>", "traffic_note": "ncu dram read+write of one launch, profiles/prefill_cfg2_ncu.txt", "launch_ms": t_launch * 1e3},
         "e2e": {"value": total_flops * e2e_steps / e2e_elapsed / 1e12, "unit": "TFLOP/s",
                 "h2d_bytes_per_step": in_bytes, "d2h_bytes_per_step": q.numel() * 2,
                 "ms_per_step": e2e_elapsed / e2e_steps * 1e3,
@@ -685,7 +745,7 @@ def run_ours(args) -> None:
             line["model_decode"] = {"error": repr(e)[:300]}
     if world == 1 and not args.no_cpu_baseline:
         threads = os.cpu_count() or 1
-        rate, done, wall = cpu_sample(bitmap.cpu(), args.cpu_seconds, 64, threads)
+        rate, done, wall = cpu_sample(global_bitmap(), args.cpu_seconds, 64, threads)
         line["cpu_baseline"] = {"value": rate, "unit": "TFLOP/s", "cores": threads, "kind": "port",
                                 "sample": f"{done} (b,h) slices of S=8192 (masked-dense fp32, reference "
                                           f"algorithm restated), {wall:.1f} s"}

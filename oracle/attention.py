@@ -18,10 +18,10 @@ import torch
 from .patterns import token_mask_from_csr
 
 
-def _causal_keep(T_q: int, T_k: int) -> torch.Tensor:
+def _causal_keep(T_q: int, T_k: int, device="cpu") -> torch.Tensor:
     # utils.py:6-12 builds triu(ones(T_k, T_k), 1) = forbidden; masked_sdpa.py:40-45
     # keeps the last row for decode (T_q == 1) and the whole square otherwise.
-    c = torch.triu(torch.ones(T_k, T_k, dtype=torch.bool), diagonal=1)
+    c = torch.triu(torch.ones(T_k, T_k, dtype=torch.bool, device=device), diagonal=1)
     if T_q == 1:
         return ~c[-1:, :]
     return ~c
@@ -41,7 +41,7 @@ def masked_sdpa(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, mask: torch.T
     T_k = k.size(2)
     scale = 1.0 / math.sqrt(D)
     scores = torch.matmul(q, k.transpose(-2, -1)) * scale
-    combined = mask.unsqueeze(0) & _causal_keep(T_q, T_k).unsqueeze(0).unsqueeze(0)
+    combined = mask.unsqueeze(0) & _causal_keep(T_q, T_k, mask.device).unsqueeze(0).unsqueeze(0)
     scores = scores.masked_fill(~combined, float("-inf"))
     attn = torch.softmax(scores, dim=-1)
     attn = torch.nan_to_num(attn, nan=0.0)

@@ -26,34 +26,42 @@ from .patterns import bigbird_csr, bigbird_token_mask
 
 
 def _rms(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
-    return x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + eps) * w
+    # Qwen3RMSNorm: normalise in fp32, back to the activation dtype, times the weight
+    xf = x.float()
+    return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)).to(x.dtype) * w
 
 
 def _rope(x: torch.Tensor, theta: float, offset: int = 0) -> torch.Tensor:
+    # apply_rotary_pos_emb: fp32 angles, cos/sin in the activation dtype
     T, D = x.shape[-2], x.shape[-1]
-    inv = 1.0 / theta ** (torch.arange(0, D, 2, dtype=torch.float32) / D)
-    ang = torch.outer(torch.arange(offset, offset + T, dtype=torch.float32), inv)
+    inv = 1.0 / theta ** (torch.arange(0, D, 2, dtype=torch.float32, device=x.device) / D)
+    ang = torch.outer(torch.arange(offset, offset + T, dtype=torch.float32, device=x.device), inv)
     emb = torch.cat([ang, ang], -1)
     rot = torch.cat([-x[..., D // 2:], x[..., : D // 2]], -1)
-    return x * emb.cos() + rot * emb.sin()
+    return x * emb.cos().to(x.dtype) + rot * emb.sin().to(x.dtype)
 
 
 @torch.no_grad()
-def masked_dense_forward(weights, tokens: torch.Tensor, layout, sparse_layers=None, cache=None) -> torch.Tensor:
+def masked_dense_forward(weights, tokens: torch.Tensor, layout, sparse_layers=None, cache=None,
+                         device="cpu", dtype=torch.float32) -> torch.Tensor:
     """Logits of the last position [B, vocab] (fp32) for ``tokens`` [B, T_new]
     appended to ``cache`` (a list of per-layer (k, v) fp32 tensors [B, Hkv, T, D],
     extended in place; None = empty prompt). Weights are a one-rank set (fields as
     in sparseattentioninfer_b200.tp.Qwen3TPWeights, world 1). Sparse layers use the
     BigBird token mask of (T_new, T_total) as the hook builds it; the others dense
-    causal attention."""
+    causal attention. ``device`` only says where the torch arithmetic runs (a
+    full-width model checks faster on a GPU); the computation is the same.
+    ``dtype`` bfloat16 runs the same model with bf16 weights and activations (the
+    reference model as deployed; attention scores and softmax stay fp32, as in
+    masked_sdpa), to size the rounding error of bf16 itself."""
     A = weights.arch
-    f = lambda t: t.detach().float().cpu()  # noqa: E731
+    f = lambda t: t.detach().to(device=device, dtype=dtype)  # noqa: E731
     B, T = tokens.shape
     H, Hkv, D = A.heads, A.kv_heads, A.head_dim
     rep = H // Hkv
     past = 0 if not cache else cache[0][0].shape[2]
-    x = f(weights.embed)[tokens.cpu()]
-    mask = bigbird_token_mask([tuple(layout)], H, T, past + T)
+    x = f(weights.embed)[tokens.to(device)]
+    mask = torch.as_tensor(bigbird_token_mask([tuple(layout)], H, T, past + T)).to(device)
     sparse = set(range(A.layers)) if sparse_layers is None else set(sparse_layers)
     for li, L in enumerate(weights.layers):
         h = _rms(x, f(L["ln1"]), A.eps)
@@ -72,18 +80,19 @@ def masked_dense_forward(weights, tokens: torch.Tensor, layout, sparse_layers=No
                 cache[li] = (k, v)
         kr, vr = k.repeat_interleave(rep, 1), v.repeat_interleave(rep, 1)
         if li in sparse:
-            att = masked_sdpa(q, kr, vr, mask, "mask")
+            att = masked_sdpa(q, kr, vr, mask, "mask").to(dtype)
         elif T == 1:
-            att = masked_sdpa(q, kr, vr, torch.ones(H, 1, kr.shape[2], dtype=torch.bool), "mask")
+            att = masked_sdpa(q, kr, vr, torch.ones(H, 1, kr.shape[2], dtype=torch.bool, device=device), "mask")
         else:
-            att = masked_sdpa(q, kr, vr, torch.ones(H, T, kr.shape[2], dtype=torch.bool), "mask")
+            att = masked_sdpa(q, kr, vr, torch.ones(H, T, kr.shape[2], dtype=torch.bool, device=device), "mask")
+        att = att.to(dtype)
         x = x + att.transpose(1, 2).reshape(B, T, H * D) @ f(L["o"]).t()
         h = _rms(x, f(L["ln2"]), A.eps)
         gu = h @ f(L["gu"]).t()
         inter = gu.shape[-1] // 2
         x = x + (F.silu(gu[..., :inter]) * gu[..., inter:]) @ f(L["down"]).t()
     x = _rms(x[:, -1], f(weights.final_norm), A.eps)
-    return x @ f(weights.lm_head).t()
+    return (x @ f(weights.lm_head).t()).float().cpu()
 
 
 def masked_dense_last_logits(weights, tokens: torch.Tensor, layout, sparse_layers=None) -> torch.Tensor:

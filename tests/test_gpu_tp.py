@@ -1,9 +1,15 @@
 """Tensor-parallel Qwen3 runner on the CUDA kernels (one rank) against the
 masked-dense fp32 oracle model: last-position logits after a chunked prefill and
-after each greedy decode step.
+after each decode step.
 
-Logits tolerance (bf16 model vs fp32 reference arithmetic): max-abs deviation
-<= 5e-2 * max|reference logit| and mean-abs <= 1e-2 * max|reference logit|."""
+Logits tolerance (bf16 model vs fp32 reference arithmetic), per position:
+max-abs deviation <= 2e-2 * max|reference logit|, mean-abs <= 4e-3 * max|reference
+logit|, and the top-1 token equal to the reference's in at least 90% of the
+(position, batch row) pairs. bf16 rounds each stored activation to 2^-8 relative;
+over a few layers that leaves per-logit deviations of ~1% of the logit range,
+which is what these bounds allow. Decode tokens are teacher-forced (the same ids
+in both runs) so that one near-tie flip does not change every later position.
+The deviations measured are printed (pytest -s)."""
 from __future__ import annotations
 
 import pytest
@@ -14,7 +20,41 @@ from sparseattentioninfer_b200 import _capi, tp
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda:0"
-MAX_REL, MEAN_REL = 5e-2, 1e-2
+MAX_REL, MEAN_REL, TOP1 = 2e-2, 4e-3, 0.9
+
+
+def _compare(got, ref, what):
+    agree = total = 0
+    worst_max = worst_mean = 0.0
+    for i, (a, b) in enumerate(zip(got, ref)):
+        scale = b.abs().max().item()
+        err = (a - b).abs()
+        worst_max = max(worst_max, err.max().item() / scale)
+        worst_mean = max(worst_mean, err.mean().item() / scale)
+        assert err.max().item() <= MAX_REL * scale and err.mean().item() <= MEAN_REL * scale, \
+            f"{what} position {i}: max {err.max().item():.3e} mean {err.mean().item():.3e} scale {scale:.3e}"
+        agree += int((a.argmax(-1) == b.argmax(-1)).sum())
+        total += a.shape[0]
+    print(f"{what}: max-abs/max|logit| {worst_max:.2e}, mean-abs/max|logit| {worst_mean:.2e}, "
+          f"top-1 agreement {agree}/{total}")
+    assert agree >= TOP1 * total, f"{what}: top-1 agreement {agree}/{total}"
+
+
+def _run_pair(A, w, layout, sparse_layers, T, chunk, steps, batch=2, seed=3):
+    r = tp.Qwen3TPRunner(w, batch, T + steps, layout, sparse_layers=sparse_layers)
+    tok = torch.randint(0, A.vocab, (batch, T), generator=torch.Generator().manual_seed(seed))
+    feed = torch.randint(0, A.vocab, (steps, batch, 1), generator=torch.Generator().manual_seed(seed + 1))
+    got = [r.prefill(tok.to(DEV), chunk=chunk).cpu()]
+    for i in range(steps):
+        _, lg = r.step(feed[i].to(DEV), return_logits=True)
+        got.append(lg.cpu())
+    torch.cuda.synchronize()
+    del r
+    cache = []
+    ref = [masked_dense_forward(w, tok, layout, sparse_layers, cache, device=DEV)]
+    for i in range(steps):
+        ref.append(masked_dense_forward(w, feed[i], layout, sparse_layers, cache, device=DEV))
+    return got, ref
 
 
 @pytest.mark.parametrize("layout,sparse_layers,T,chunk", [
@@ -24,26 +64,47 @@ MAX_REL, MEAN_REL = 5e-2, 1e-2
 def test_tp1_runner_logits_vs_masked_dense(layout, sparse_layers, T, chunk):
     A = tp.Qwen3Arch(hidden=512, layers=2, heads=32, kv_heads=8, head_dim=128, intermediate=1024, vocab=2000)
     w = tp.Qwen3TPWeights(A, 0, 1, seed=7, device=DEV)
-    steps = 6
-    r = tp.Qwen3TPRunner(w, 2, T + steps, layout, sparse_layers=sparse_layers)
-    tok = torch.randint(0, A.vocab, (2, T), generator=torch.Generator().manual_seed(3))
-    got = [r.prefill(tok.to(DEV), chunk=chunk).cpu()]
-    t = got[0].argmax(-1, keepdim=True)
-    feed = [t]
-    for _ in range(steps):
-        t, lg = r.step(t.to(DEV), return_logits=True)
-        got.append(lg.cpu())
-        feed.append(t.cpu())
-    torch.cuda.synchronize()
+    got, ref = _run_pair(A, w, layout, sparse_layers, T, chunk, steps=6)
+    _compare(got, ref, f"reduced model {layout}")
+    assert _capi.device_error() == 0
+
+
+def test_config5_full_width_full_depth_logits():
+    """Config 5's architecture at full width and depth (Qwen3-8B: hidden 4096, 36
+    layers, 32/8 heads, SwiGLU 12288, vocab 151936; BigBird (128, 2, 4, 3) in every
+    layer) on a reduced context (batch 2, 2048-token prompt, 4 decode steps): the
+    runner's bf16 logits against the masked-dense fp32 oracle model with the same
+    weights and token ids. Over 36 bf16 layers rounding alone moves logits by a
+    few percent of their range, so the bound is relative to the reference model
+    itself run in bf16 (the same masked-dense arithmetic with bf16 weights and
+    activations, as the reference deploys it): the runner's deviation from fp32
+    may be at most 1.5x the bf16 reference's, and its top-1 agreement with fp32
+    at most one (position, row) pair below the bf16 reference's."""
+    A = tp.QWEN3_8B
+    w = tp.Qwen3TPWeights(A, 0, 1, seed=0, device=DEV)
+    layout, T, steps, batch = (128, 2, 4, 3), 2048, 4, 2
+    got, ref = _run_pair(A, w, layout, None, T, 1024, steps, batch=batch)
+    tok = torch.randint(0, A.vocab, (batch, T), generator=torch.Generator().manual_seed(3))
+    feed = torch.randint(0, A.vocab, (steps, batch, 1), generator=torch.Generator().manual_seed(4))
     cache = []
-    ref = [masked_dense_forward(w, tok, layout, sparse_layers, cache)]
-    for t in feed[:-1]:
-        ref.append(masked_dense_forward(w, t.cpu(), layout, sparse_layers, cache))
-    for i, (a, b) in enumerate(zip(got, ref)):
-        scale = b.abs().max().item()
-        err = (a - b).abs()
-        assert err.max().item() <= MAX_REL * scale and err.mean().item() <= MEAN_REL * scale, \
-            f"position {i}: max {err.max().item():.3e} mean {err.mean().item():.3e} scale {scale:.3e}"
+    bf = [masked_dense_forward(w, tok, layout, None, cache, device=DEV, dtype=torch.bfloat16)]
+    for i in range(steps):
+        bf.append(masked_dense_forward(w, feed[i], layout, None, cache, device=DEV, dtype=torch.bfloat16))
+    del cache, w
+    torch.cuda.empty_cache()
+
+    def stats(xs):
+        dmax = max(((a - b).abs().max() / b.abs().max()).item() for a, b in zip(xs, ref))
+        dmean = max(((a - b).abs().mean() / b.abs().max()).item() for a, b in zip(xs, ref))
+        top1 = sum(int((a.argmax(-1) == b.argmax(-1)).sum()) for a, b in zip(xs, ref))
+        return dmax, dmean, top1
+
+    ours, theirs = stats(got), stats(bf)
+    n = batch * (steps + 1)
+    print(f"config 5 full width vs fp32: runner max {ours[0]:.2e} mean {ours[1]:.2e} top-1 {ours[2]}/{n}; "
+          f"bf16 reference max {theirs[0]:.2e} mean {theirs[1]:.2e} top-1 {theirs[2]}/{n}")
+    assert ours[0] <= 1.5 * theirs[0] and ours[1] <= 1.5 * theirs[1], (ours, theirs)
+    assert ours[2] >= theirs[2] - 1, (ours, theirs)
     assert _capi.device_error() == 0
 
 
