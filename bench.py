@@ -485,6 +485,48 @@ def time_tp_model(device, rank: int, world: int, *, prompt=65536, steps=512, bat
     return res
 
 
+def tp_parity(device, rank: int, world: int) -> dict | None:
+    """Numerics of the tensor-parallel path at this world size, on every rank: a
+    reduced Qwen3 (hidden 512, 2 layers, 32/8 heads, BigBird (128, 2, 4, 3))
+    prefills 1280 tokens and decodes 6 teacher-forced steps eagerly and 6 more
+    from the captured CUDA graph with TP-N (fused NVLink all-reduce for decode,
+    NCCL for prefill); rank 0 runs the same model on one GPU (TP-1, same
+    weights: drawn per full matrix) and compares the 13 last-position logits.
+    Returns max-abs deviation / max|logit| and top-1 agreement (rank 0)."""
+    from sparseattentioninfer_b200 import tp
+    from sparseattentioninfer_b200.comm import NvlinkAllReduce
+    A = tp.Qwen3Arch(hidden=512, layers=2, heads=32, kv_heads=8, head_dim=128, intermediate=1024, vocab=2000)
+    layout, T, steps = (128, 2, 4, 3), 1280, 6
+    tok = torch.randint(0, A.vocab, (2, T), generator=torch.Generator().manual_seed(8)).to(device)
+    feed = torch.randint(0, A.vocab, (2 * steps, 2, 1), generator=torch.Generator().manual_seed(9)).to(device)
+    solo = torch.distributed.new_group([0]) if world > 1 else None
+
+    def run(w, comm, group):
+        r = tp.Qwen3TPRunner(w, 2, T + 2 * steps, layout, comm=comm, group=group)
+        out = [r.prefill(tok, chunk=512).float().cpu()]
+        for i in range(steps):
+            out.append(r.step(feed[i], return_logits=True)[1].float().cpu())
+        r.capture_decode()
+        for i in range(steps):
+            r.step_graph(feed[steps + i])
+            out.append(r.graph_logits.float().cpu())
+        torch.cuda.synchronize()
+        return out
+
+    comm = NvlinkAllReduce(64 * 1024, device=device) if world > 1 else None
+    got = run(tp.Qwen3TPWeights(A, rank, world, seed=21, device=device), comm, None)
+    if comm is not None:
+        comm.close()
+    if rank != 0:
+        return None
+    ref = run(tp.Qwen3TPWeights(A, 0, 1, seed=21, device=device), None, solo)
+    dev = max(((a - b).abs().max() / b.abs().max()).item() for a, b in zip(got, ref))
+    top1 = sum(int((a.argmax(-1) == b.argmax(-1)).sum()) for a, b in zip(got, ref))
+    return {"what": f"TP-{world} vs TP-1 logits, reduced Qwen3 (hidden 512, 2 layers), prefill {T} + "
+                    f"{steps} eager + {steps} graph decode steps (teacher-forced), 2 rows",
+            "max_abs_dev_rel": dev, "top1_agree": top1, "top1_total": 2 * len(got)}
+
+
 def time_qwen3_decode(device, layers=36, batch=32, ctx=32768, steps=256, chunk=1024, sparse_layers=18,
                       seed=0) -> dict:
     """Config 4: random-init Qwen3-4B architecture (hidden 2560, 36 layers, 32/8 heads,
@@ -673,6 +715,13 @@ def run_ours(args) -> None:
         torch.distributed.all_reduce(fl)
         gqa["ms_max_over_ranks"] = float(gt.item())
         gqa["tflops_all_ranks"] = float(fl.item()) / (float(gt.item()) * 1e-3) / 1e12
+    parity = None
+    if world > 1:
+        try:
+            parity = tp_parity(device, rank, world)
+        except Exception as e:  # noqa: BLE001
+            parity = {"error": repr(e)[:300]}
+        torch.distributed.barrier()
     tp_model = None
     if args.tp_model == "on":
         try:
@@ -732,6 +781,8 @@ def run_ours(args) -> None:
     except Exception as e:  # noqa: BLE001
         line["decode"] = {"error": repr(e)}
     line["gqa_layer"] = gqa
+    if parity is not None:
+        line["tp_parity"] = parity
     if tp_model is not None:
         line["tp_model"] = tp_model
     if args.model != "off" and world == 1:

@@ -122,6 +122,19 @@ SA_API int sa_bitmap_pairs(const uint8_t* bitmap, int32_t H, int32_t NQB, int32_
                     const int32_t* offsets, int32_t* pairs, int32_t max_pairs,
                     sa_stream_t stream);
 
+/* CSR validation: the properties the attention kernels rely on. Per head h of
+ * pairs [H, pairs_stride] / offsets [H, NQB+1]: offsets[h, 0] == 0, offsets
+ * non-decreasing and <= pairs_stride, every block index of row q in [0, NKB)
+ * and strictly increasing along the row (the reference's builders emit sorted
+ * rows: build_block_pairs_from_mask takes nonzero() of each row,
+ * sparse_attentions/patterns/base.py:75-89; _get_block_pairs sorts each row,
+ * bigbird_pattern.py:533-583). `result` is 4 int32 of device scratch. Blocks
+ * until done (one device->host read). Returns SA_ERR_CSR and names the first
+ * violation in sa_last_error() when invalid. Replaces the reference wrapper's
+ * host-side input checks (kernels/triton/universal_sparse_attn.py:187-199). */
+SA_API int sa_validate_csr(const int32_t* pairs, const int32_t* offsets, int32_t H, int32_t NQB, int32_t NKB,
+                           int32_t pairs_stride, int32_t* result, sa_stream_t stream);
+
 /* Legacy padded schedule -> CSR. Replaces kv_block_list_to_pairs
  * (sparse_attentions/patterns/base.py:92-133): kv_block_list [H, NQB, MAX_KV]
  * int32 with -1 padding. Same two-phase protocol. */

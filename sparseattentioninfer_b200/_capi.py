@@ -23,6 +23,7 @@ EXPORTED = (
     "sa_block_bitmap_from_token_mask",
     "sa_bitmap_offsets",
     "sa_bitmap_pairs",
+    "sa_validate_csr",
     "sa_kvlist_offsets",
     "sa_kvlist_pairs",
     "sa_prefill_fwd",
@@ -126,6 +127,7 @@ def load(path: str | os.PathLike | None = None) -> ctypes.CDLL:
     lib.sa_block_bitmap_from_token_mask.argtypes = [_c_p, _c_i32, _c_i32, _c_i32, _c_i32, _c_p, _c_p]
     lib.sa_bitmap_offsets.argtypes = [_c_p, _c_i32, _c_i32, _c_i32, _c_p, _c_p]
     lib.sa_bitmap_pairs.argtypes = [_c_p, _c_i32, _c_i32, _c_i32, _c_p, _c_p, _c_i32, _c_p]
+    lib.sa_validate_csr.argtypes = [_c_p, _c_p, _c_i32, _c_i32, _c_i32, _c_i32, _c_p, _c_p]
     lib.sa_kvlist_offsets.argtypes = [_c_p, _c_i32, _c_i32, _c_i32, _c_p, _c_p]
     lib.sa_kvlist_pairs.argtypes = [_c_p, _c_i32, _c_i32, _c_i32, _c_p, _c_p, _c_i32, _c_p]
     lib.sa_prefill_fwd.argtypes = [ctypes.POINTER(AttnArgs), _c_p]

@@ -12,6 +12,7 @@ and ``actual_backend`` is always "cuda_sm100".
 from __future__ import annotations
 
 import math
+import weakref
 from abc import ABC, abstractmethod
 
 import torch
@@ -24,6 +25,21 @@ class AttentionBackend(ABC):
     """sparse_attentions/attention/base.py:9-40."""
 
     @abstractmethod
+    def _validate(self, pairs, offsets, T_q: int, T_k: int, bs: int) -> None:
+        """A CSR from outside this package (e.g. the reference's own pattern
+        objects) is validated once per tensor pair and contents (sa_validate_csr;
+        the tensors are held by weak reference, their in-place version counters
+        detect changes); a violation raises SaError (SA_ERR_CSR)."""
+        key = (id(pairs), id(offsets), T_q, T_k, bs)
+        hit = self._validated.get(key)
+        if hit is not None and hit[0]() is pairs and hit[1]() is offsets and \
+                hit[2] == (pairs._version, offsets._version):
+            return
+        _ops.validate_csr(pairs, offsets, T_q, T_k, bs)
+        self._validated[key] = (weakref.ref(pairs), weakref.ref(offsets), (pairs._version, offsets._version))
+        while len(self._validated) > 64:
+            self._validated.pop(next(iter(self._validated)))
+
     def forward(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, pattern: PatternMetadata) -> torch.Tensor:
         ...
 
@@ -52,6 +68,7 @@ class CudaSm100Backend(AttentionBackend):
         self.dense_block_size = dense_block_size
         self._dense_cache: dict = {}
         self._mask_cache: dict = {}
+        self._validated: dict = {}
         self._last = "cuda_sm100"
 
     @property
@@ -72,6 +89,21 @@ class CudaSm100Backend(AttentionBackend):
                 self._dense_cache.pop(next(iter(self._dense_cache)))
         return self._dense_cache[key]
 
+    def _validate(self, pairs, offsets, T_q: int, T_k: int, bs: int) -> None:
+        """A CSR from outside this package (e.g. the reference's own pattern
+        objects) is validated once per tensor pair and contents (sa_validate_csr;
+        the tensors are held by weak reference, their in-place version counters
+        detect changes); a violation raises SaError (SA_ERR_CSR)."""
+        key = (id(pairs), id(offsets), T_q, T_k, bs)
+        hit = self._validated.get(key)
+        if hit is not None and hit[0]() is pairs and hit[1]() is offsets and \
+                hit[2] == (pairs._version, offsets._version):
+            return
+        _ops.validate_csr(pairs, offsets, T_q, T_k, bs)
+        self._validated[key] = (weakref.ref(pairs), weakref.ref(offsets), (pairs._version, offsets._version))
+        while len(self._validated) > 64:
+            self._validated.pop(next(iter(self._validated)))
+
     def forward(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, pattern: PatternMetadata) -> torch.Tensor:
         if not q.is_cuda:
             raise RuntimeError("cuda_sm100 backend needs CUDA tensors (no CPU fallback)")
@@ -90,6 +122,8 @@ class CudaSm100Backend(AttentionBackend):
                 pairs, offsets = self._mask_cache[key]
             if bs is None:
                 raise ValueError("pattern.block_size is None")
+            if not getattr(pattern, "_sa_compiled", False) and pattern.block_pairs is not None:
+                self._validate(pairs, offsets, T_q, T_k, int(bs))
         elif pattern.kind == "topk":
             self._last = "cuda_sm100"
             return _ops.topk_attention(q, k, v, int(pattern.topk))

@@ -319,6 +319,71 @@ static int fill_bigbird(BigBirdParams* P, const sa_bigbird_layout* layouts, int 
 
 using namespace sa;
 
+// ---------------------------------------------------------------------------
+// CSR validation (the checks the attention kernels rely on)
+// ---------------------------------------------------------------------------
+// One CTA per head, one thread per row: offsets[h, 0] == 0, non-decreasing,
+// offsets[h, NQB] <= pairs_stride; every index of a row in [0, NKB) and strictly
+// increasing. The first violation found (by any thread) is recorded in
+// result[0..3] = (kind, head, row, position); kind 0 = valid.
+__global__ void validate_csr_kernel(const int32_t* __restrict__ pairs, const int32_t* __restrict__ offsets,
+                                    int NQB, int NKB, int stride, int32_t* result) {
+  const int h = blockIdx.x;
+  const int32_t* off = offsets + (int64_t)h * (NQB + 1);
+  const int32_t* row = pairs + (int64_t)h * stride;
+  auto fail = [&](int kind, int r, int pos) {
+    if (atomicCAS(result, 0, kind) == 0) {
+      result[1] = h;
+      result[2] = r;
+      result[3] = pos;
+    }
+  };
+  if (threadIdx.x == 0 && __ldg(off) != 0) fail(1, 0, 0);
+  for (int r = threadIdx.x; r < NQB; r += blockDim.x) {
+    const int o0 = __ldg(off + r), o1 = __ldg(off + r + 1);
+    if (o1 < o0) {
+      fail(2, r, o0);
+      continue;
+    }
+    if (o1 > stride || o0 < 0) {
+      fail(3, r, o1);
+      continue;
+    }
+    int prev = -1;
+    for (int i = o0; i < o1; ++i) {
+      const int kb = __ldg(row + i);
+      if (kb < 0 || kb >= NKB) {
+        fail(4, r, i);
+        break;
+      }
+      if (kb <= prev) {
+        fail(5, r, i);
+        break;
+      }
+      prev = kb;
+    }
+  }
+}
+
+extern "C" int sa_validate_csr(const int32_t* pairs, const int32_t* offsets, int32_t H, int32_t NQB, int32_t NKB,
+                               int32_t pairs_stride, int32_t* result, sa_stream_t stream) {
+  if (!pairs || !offsets || !result || H <= 0 || NQB <= 0 || NKB <= 0 || pairs_stride <= 0)
+    return sa_fail(SA_ERR_INVALID, "bad arguments");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  SA_CHECK_CUDA(cudaMemsetAsync(result, 0, 4 * sizeof(int32_t), s));
+  validate_csr_kernel<<<H, 128, 0, s>>>(pairs, offsets, NQB, NKB, pairs_stride, result);
+  SA_CHECK_CUDA(cudaGetLastError());
+  int32_t host[4] = {0, 0, 0, 0};
+  SA_CHECK_CUDA(cudaMemcpyAsync(host, result, sizeof(host), cudaMemcpyDeviceToHost, s));
+  SA_CHECK_CUDA(cudaStreamSynchronize(s));
+  static const char* what[] = {"", "offsets[h, 0] != 0", "offsets decrease", "offset outside [0, pairs_stride]",
+                               "block index outside [0, NKB)", "row not strictly increasing"};
+  if (host[0] != 0)
+    return sa_fail(SA_ERR_CSR, "invalid CSR: %s (head %d, row %d, position %d)",
+                   what[host[0] >= 1 && host[0] <= 5 ? host[0] : 0], host[1], host[2], host[3]);
+  return SA_OK;
+}
+
 extern "C" int sa_bigbird_offsets(const sa_bigbird_layout* layouts, int32_t n_groups, int32_t n_heads,
                                   int32_t T_q, int32_t T_k, int32_t block_size, int32_t variant,
                                   int32_t* offsets, sa_stream_t stream) {

@@ -12,6 +12,8 @@ call into ``libsa_b200.so``:
     torch.ops.cuda_sparse_attention.compile_token_mask(mask, block_size)
     torch.ops.cuda_sparse_attention.compile_kv_block_list(kv_block_list)
     torch.ops.cuda_sparse_attention.compile_bigbird(layouts, n_heads, T_q, T_k, block_size, variant, like)
+    torch.ops.cuda_sparse_attention.cuda_bigbird_sparse_attention(q, k, v, block_size=64, global_blocks=2,
+                                                                  sliding_blocks=3, random_blocks=2)
 
 The plain functions below are the same entry points without dispatcher
 overhead; the backend uses them. Nothing here has a CPU path: non-CUDA
@@ -141,6 +143,28 @@ def block_bitmap_from_token_mask(mask: torch.Tensor, block_size: int) -> torch.T
 def compile_token_mask(mask: torch.Tensor, block_size: int) -> tuple[torch.Tensor, torch.Tensor]:
     """build_block_pairs_from_mask (patterns/base.py:36-89) on the device."""
     return compile_block_bitmap(block_bitmap_from_token_mask(mask, block_size))
+
+
+def validate_csr(block_pairs: torch.Tensor, block_pair_offsets: torch.Tensor, T_q: int, T_k: int,
+                 block_size: int) -> None:
+    """Checks a caller-supplied CSR the way the kernels need it (sa_validate_csr):
+    offsets start at 0, never decrease and stay within the pairs width; block
+    indices lie in [0, ceil(T_k / block_size)) and strictly increase along each
+    row. Raises SaError (SA_ERR_CSR) naming the first violation. One device->host
+    read."""
+    _require_cuda(block_pairs, block_pair_offsets)
+    if block_pairs.dtype != torch.int32 or block_pair_offsets.dtype != torch.int32:
+        raise TypeError("block_pairs / block_pair_offsets must be int32")
+    H = block_pairs.size(0)
+    nqb, nkb = math.ceil(T_q / block_size), math.ceil(T_k / block_size)
+    if block_pair_offsets.shape != (H, nqb + 1) or block_pairs.stride(1) != 1 or \
+            not block_pair_offsets.is_contiguous():
+        raise ValueError(f"offsets must be contiguous [H, {nqb + 1}] and pairs row-contiguous")
+    res = torch.empty(4, dtype=torch.int32, device=block_pairs.device)
+    with torch.cuda.device(block_pairs.device):
+        _capi.check(_capi.load().sa_validate_csr(block_pairs.data_ptr(), block_pair_offsets.data_ptr(), H, nqb, nkb,
+                                                 block_pairs.stride(0), res.data_ptr(),
+                                                 _stream(block_pairs.device)))
 
 
 def compile_kv_block_list(kv_block_list: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
@@ -413,6 +437,8 @@ _LIB.define("prefill_fwd(Tensor q, Tensor k, Tensor v, Tensor block_pairs, Tenso
             "int block_size, float? scale=None) -> Tensor")
 _LIB.define("decode_fwd(Tensor q, Tensor k, Tensor v, Tensor block_pairs, Tensor block_pair_offsets, "
             "int block_size, float? scale=None, int? n_split=None) -> Tensor")
+_LIB.define("cuda_bigbird_sparse_attention(Tensor q, Tensor k, Tensor v, int block_size=64, int global_blocks=2, "
+            "int sliding_blocks=3, int random_blocks=2) -> Tensor")
 _LIB.define("compile_block_bitmap(Tensor bitmap) -> (Tensor, Tensor)")
 _LIB.define("compile_token_mask(Tensor mask, int block_size) -> (Tensor, Tensor)")
 _LIB.define("compile_kv_block_list(Tensor kv_block_list) -> (Tensor, Tensor)")
@@ -432,6 +458,32 @@ def _op_decode(q, k, v, p, o, bs, scale=None, n_split=None):
     return decode_fwd(q, k, v, p, o, bs, scale=scale, n_split=n_split)
 
 
+def cuda_bigbird_sparse_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, block_size: int = 64,
+                                  global_blocks: int = 2, sliding_blocks: int = 3,
+                                  random_blocks: int = 2) -> torch.Tensor:
+    """The op the reference reserves for a native BigBird kernel
+    (``cuda_bigbird_sparse_attention(q, k, v)``, commented out at
+    kernels/cuda/src/torch_wrappers/ops.py:34-62): BigBird attention with the
+    reference's block rule (global blocks, a sliding window ending at the
+    diagonal block, random blocks rotated per query head,
+    bigbird_pattern.py:23-41, 533-583), causal, scale 1/sqrt(D). The layout
+    defaults are the CPU-runnable configuration's (64, 2, 3, 2). q/k/v as in
+    sparse_attn (k/v may have fewer heads: GQA). The CSR is compiled on the
+    device per (T_q, T_k) and cached."""
+    layout = (int(block_size), int(global_blocks), int(sliding_blocks), int(random_blocks))
+    key = (q.size(1), q.size(2), k.size(2), layout, str(q.device))
+    hit = _BIGBIRD_OP_CACHE.get(key)
+    if hit is None:
+        hit = compile_bigbird([layout], q.size(1), q.size(2), k.size(2), layout[0], device=q.device)
+        _BIGBIRD_OP_CACHE[key] = hit
+        while len(_BIGBIRD_OP_CACHE) > 16:
+            _BIGBIRD_OP_CACHE.pop(next(iter(_BIGBIRD_OP_CACHE)))
+    return sparse_attn(q, k, v, hit[0], hit[1], layout[0])
+
+
+_BIGBIRD_OP_CACHE: dict = {}
+
+
 def _op_bigbird(layouts, n_heads, T_q, T_k, bs, variant, like):
     lay = [tuple(layouts[i:i + 4]) for i in range(0, len(layouts), 4)]
     return compile_bigbird(lay, n_heads, T_q, T_k, bs, variant=variant, device=like.device)
@@ -440,10 +492,21 @@ def _op_bigbird(layouts, n_heads, T_q, T_k, bs, variant, like):
 _LIB.impl("sparse_attn", _op_sparse_attn, "CUDA")
 _LIB.impl("prefill_fwd", _op_prefill, "CUDA")
 _LIB.impl("decode_fwd", _op_decode, "CUDA")
+_LIB.impl("cuda_bigbird_sparse_attention", cuda_bigbird_sparse_attention, "CUDA")
 _LIB.impl("compile_block_bitmap", compile_block_bitmap, "CUDA")
 _LIB.impl("compile_token_mask", compile_token_mask, "CUDA")
 _LIB.impl("compile_kv_block_list", compile_kv_block_list, "CUDA")
 _LIB.impl("compile_bigbird", _op_bigbird, "CUDA")
+
+@torch.library.register_fake("cuda_sparse_attention::cuda_bigbird_sparse_attention", lib=_LIB)
+def _fake_bigbird(q, k, v, block_size=64, global_blocks=2, sliding_blocks=3, random_blocks=2):  # noqa: ARG001
+    torch._check(q.dim() == 4 and k.dim() == 4 and v.dim() == 4)
+    torch._check(q.device == k.device and q.device == v.device)
+    torch._check(q.dtype == k.dtype and q.dtype == v.dtype)
+    torch._check(q.shape[0] == k.shape[0] == v.shape[0])
+    torch._check(k.shape[2] == v.shape[2] and q.shape[3] == k.shape[3] == v.shape[3])
+    return torch.empty_like(q)
+
 
 for _name in ("sparse_attn", "prefill_fwd", "decode_fwd"):
     def _fake(q, k, v, p, o, bs, scale=None, n_split=None):  # noqa: ARG001

@@ -43,6 +43,13 @@ class PatternMetadata:
     block_pair_offsets: torch.Tensor | None = None
 
 
+def _compiled(md: PatternMetadata) -> PatternMetadata:
+    """Marks a CSR produced by this package's device compiler: the backend skips
+    its one-time validation (sa_validate_csr) for such metadata."""
+    md._sa_compiled = True
+    return md
+
+
 class SparsePattern(ABC):
     """sparse_attentions/patterns/base.py:136-154."""
 
@@ -181,8 +188,8 @@ class _BigBirdBase(SparsePattern):
         kvl = None
         if self.build_kv_block_list:
             kvl = self._kv_block_list(pairs, offsets, layouts, T_q, T_k, bs)
-        return PatternMetadata(kind="mask", mask=mask, keep_ratio=keep, block_size=bs, kv_block_list=kvl,
-                               block_pairs=pairs, block_pair_offsets=offsets)
+        return _compiled(PatternMetadata(kind="mask", mask=mask, keep_ratio=keep, block_size=bs, kv_block_list=kvl,
+                                         block_pairs=pairs, block_pair_offsets=offsets))
 
     def _kv_block_list(self, pairs, offsets, layouts, T_q, T_k, bs):
         """Legacy padded schedule (bigbird_pattern.py:585-634) from the CSR rows."""
@@ -291,8 +298,8 @@ class BlockMaskPattern(SparsePattern):
             self._cache[key] = (pairs, offsets, keep)
         pairs, offsets, keep = self._cache[key]
         mask = _token_mask_from_csr(pairs, offsets, self.block_size, T_q, T_k, False) if self.materialize_mask else None
-        return PatternMetadata(kind="mask", mask=mask, keep_ratio=keep, block_size=self.block_size,
-                               block_pairs=pairs, block_pair_offsets=offsets)
+        return _compiled(PatternMetadata(kind="mask", mask=mask, keep_ratio=keep, block_size=self.block_size,
+                                         block_pairs=pairs, block_pair_offsets=offsets))
 
 
 class LocalWindowPattern(SparsePattern):
@@ -326,8 +333,9 @@ class LocalWindowPattern(SparsePattern):
         W = self.window_size
         qoff = max(0, T_k - T_q)
         keep = min(1.0, sum(min(W, qoff + i + 1) for i in range(T_q)) / max(1, T_q * T_k))
-        return PatternMetadata(kind="local", mask=mask if self.materialize_mask else None, keep_ratio=keep,
-                               block_size=self.block_size, block_pairs=pairs, block_pair_offsets=offsets)
+        return _compiled(PatternMetadata(kind="local", mask=mask if self.materialize_mask else None,
+                                         keep_ratio=keep, block_size=self.block_size, block_pairs=pairs,
+                                         block_pair_offsets=offsets))
 
 
 class DenseCausalPattern(SparsePattern):

@@ -106,3 +106,9 @@ def test_package_import_exposes_reference_api():
         sa.get_backend("triton_universal")
     reg = sa.register_with_reference({})
     assert reg["cuda_sm100"] is sa.CudaSm100Backend
+
+
+def test_validate_csr_host_arguments():
+    lib = _capi.load()
+    assert lib.sa_validate_csr(None, None, 1, 1, 1, 1, None, None) == _capi.SA_ERR_INVALID
+    assert lib.sa_validate_csr(1 << 20, 1 << 20, 0, 1, 1, 1, 1 << 20, None) == _capi.SA_ERR_INVALID

@@ -253,3 +253,23 @@ def test_config3_full_size_gqa_layer_heads_vs_oracle():
     for h in heads:
         assert_close(out[:, h], ref[:, h].numpy(), f"config3 head {h}")
     assert _capi.device_error() == 0
+
+
+def test_reference_built_metadata_through_forward(manifest, csr_cases):
+    """The CSR the reference's own BigBirdKeepRatioPattern built (fixture
+    cfg1_layout, made by tests/golden/make_golden.py) in an object with the
+    reference PatternMetadata's fields (not this package's class) goes through
+    forward() — validated once as a caller CSR — and matches the reference's
+    MaskedSdpaBackend output on the same inputs (fixture cfg1_rotation)."""
+    import types
+    meta = manifest["attn"]["cfg1_rotation"]
+    q, k, v = (t.to(DEV) for t in case_inputs(meta))
+    md = types.SimpleNamespace(kind="mask", mask=None, topk=None, keep_ratio=0.0, build_time_ms=0.0, block_size=64,
+                               kv_block_list=None,
+                               block_pairs=torch.from_numpy(csr_cases["cfg1_layout.pairs"]).to(DEV),
+                               block_pair_offsets=torch.from_numpy(csr_cases["cfg1_layout.offsets"]).to(DEV))
+    out = sa.get_backend("cuda_sm100").forward(q, k, v, md)
+    assert_close(out, golden_attn("cfg1_rotation"), "reference metadata")
+    out2 = torch.ops.cuda_sparse_attention.cuda_bigbird_sparse_attention(q, k, v)  # layout (64, 2, 3, 2)
+    assert_close(out2, golden_attn("cfg1_rotation"), "cuda_bigbird_sparse_attention op")
+    assert _capi.device_error() == 0
