@@ -588,8 +588,31 @@ def time_qwen3_decode(device, layers=36, batch=32, ctx=32768, steps=256, chunk=1
         torch.cuda.synchronize()
         return e0.elapsed_time(e1) / 1e3
 
+    def hook_arm(n):
+        """The reference's model API: HF Qwen3ForCausalLM with the attention hook
+        (Qwen3SparseKernelAttention) over the same weights and prefilled cache."""
+        from sparseattentioninfer_b200.qwen3 import hf_model_over_tp
+        runner.length = ctx
+        model, cache = hf_model_over_tp(runner)
+        tok = first
+        for _ in range(2):  # warm: per-shape pattern builds, cuBLAS handles
+            tok = model(input_ids=tok, past_key_values=cache, use_cache=True).logits[:, -1].argmax(-1, keepdim=True)
+        for cl in cache.layers:
+            cl.length = ctx
+        tok = first
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(n):
+            tok = model(input_ids=tok, past_key_values=cache, use_cache=True).logits[:, -1].argmax(-1, keepdim=True)
+        e1.record()
+        torch.cuda.synchronize()
+        del model, cache
+        return e0.elapsed_time(e1) / 1e3
+
     with torch.no_grad():
         t_sparse = graph_arm(steps)
+        hook_steps = min(steps, 64)
+        t_hook = hook_arm(hook_steps)
         runner.sparse = set()
         t_dense = graph_arm(steps)
         runner.dense_impl = "sdpa"
@@ -603,7 +626,10 @@ def time_qwen3_decode(device, layers=36, batch=32, ctx=32768, steps=256, chunk=1
         "sparse_ms_per_step": t_sparse / steps * 1e3, "dense_ms_per_step": t_dense / steps * 1e3,
         "dense_sdpa_ms_per_step": t_sdpa / steps * 1e3,
         "speedup_vs_dense": t_dense / t_sparse, "speedup_vs_dense_sdpa": t_sdpa / t_sparse,
-        "decode": "sparse and dense: one CUDA graph per step; dense_sdpa: eager",
+        "hook_tok_s": batch * hook_steps / t_hook, "hook_ms_per_step": t_hook / hook_steps * 1e3,
+        "hook_steps": hook_steps,
+        "decode": "sparse and dense: one CUDA graph per step; dense_sdpa: eager; hook: the HF model with "
+                  "Qwen3SparseKernelAttention (eager, the reference callers' API) from the same cache",
     })
     del runner, w
     torch.cuda.empty_cache()

@@ -167,7 +167,10 @@ class _BigBirdBase(SparsePattern):
         self.last_group_layouts = layouts
         self.last_layout = layouts[0] if len(layouts) == 1 else None
         bs = next_pow2_min16(layouts[0][0])
-        key = (T_q, T_k, _device_key(device), layouts)
+        # A decode row depends on T_k only through its block (T_k-1)//bs and the
+        # block count ceil(T_k/bs): decoding reuses one build for a whole block.
+        tk_key = ((T_k - 1) // bs, -(-T_k // bs)) if T_q == 1 else T_k
+        key = (T_q, tk_key, _device_key(device), layouts)
         if key not in self._csr_cache:
             exact = self.exact_width if self.exact_width is not None else T_q > 1
             width = None if exact else self._width_bound(layouts, T_q, T_k, bs)

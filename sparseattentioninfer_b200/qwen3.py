@@ -32,6 +32,7 @@ from transformers.cache_utils import Cache, DynamicLayer
 from transformers.models.qwen3.configuration_qwen3 import Qwen3Config
 from transformers.models.qwen3.modeling_qwen3 import Qwen3Attention, Qwen3ForCausalLM, apply_rotary_pos_emb
 
+from . import ops as _ops
 from .backend import CudaSm100Backend
 from .patterns import (
     BigBirdKeepRatioPattern,
@@ -147,6 +148,14 @@ class Qwen3SparseKernelAttention(Qwen3Attention):
         # selects PyTorch SDPA (library FlashAttention / cuDNN), the comparator
         # the reference's benchmarks call the dense path.
         self.dense_impl = _get(config, "sparse_attention_dense_impl", "cuda_sm100")
+        # The fused prologue (one projection GEMM + ops.qk_norm_rope_append) serves
+        # a PreallocatedKVCache when RoPE is the default kind and there is no bias.
+        rope = _get(config, "rope_parameters", None) or {}
+        self._rope_theta = float(rope.get("rope_theta", _get(config, "rope_theta", 10000.0)))
+        self._fusable = (rope.get("rope_type", "default") == "default" and self.q_proj.bias is None
+                         and self.head_dim in (64, 128))
+        self._qkv_cache = None
+        self._rope_tab = None
 
     @property
     def actual_backend(self) -> str:
@@ -174,19 +183,79 @@ class Qwen3SparseKernelAttention(Qwen3Attention):
             return BigBirdPattern(top_k=self.top_k, n_heads=H)
         return LocalWindowPattern(window_size=self.window_size, block_size=self.block_size, materialize_mask=False)
 
+    def _fused_qkv_weight(self) -> torch.Tensor:
+        """[Wq; Wk; Wv] as one matrix: a view when the three weights are adjacent
+        slices of one buffer (e.g. hf_model_over_tp), else a copy made once."""
+        wq, wk, wv = self.q_proj.weight, self.k_proj.weight, self.v_proj.weight
+        key = (wq.data_ptr(), wk.data_ptr(), wv.data_ptr(), wq._version, wk._version, wv._version)
+        if self._qkv_cache is not None and self._qkv_cache[0] == key:
+            return self._qkv_cache[1]
+        es = wq.element_size()
+        adjacent = (wq.is_contiguous() and wk.is_contiguous() and wv.is_contiguous()
+                    and wq.untyped_storage().data_ptr() == wk.untyped_storage().data_ptr()
+                    == wv.untyped_storage().data_ptr()
+                    and wk.data_ptr() == wq.data_ptr() + wq.numel() * es
+                    and wv.data_ptr() == wk.data_ptr() + wk.numel() * es)
+        if adjacent:
+            fused = torch.empty(0, dtype=wq.dtype, device=wq.device).set_(
+                wq.untyped_storage(), wq.storage_offset(), (wq.shape[0] + wk.shape[0] + wv.shape[0], wq.shape[1]),
+                (wq.shape[1], 1))
+        else:
+            fused = torch.cat([wq, wk, wv], 0)
+        self._qkv_cache = (key, fused)
+        return fused
+
+    def _rope_tables(self, capacity: int, device, dtype):
+        """cos / sin [capacity, D] of the default RoPE (fp32 angles, stored in the
+        activation dtype), as apply_rotary_pos_emb uses them."""
+        t = self._rope_tab
+        if t is None or t[0].shape[0] < capacity or t[0].device != device or t[0].dtype != dtype:
+            D = self.head_dim
+            inv = 1.0 / self._rope_theta ** (torch.arange(0, D, 2, device=device, dtype=torch.float32) / D)
+            ang = torch.outer(torch.arange(capacity, device=device, dtype=torch.float32), inv)
+            emb = torch.cat([ang, ang], -1)
+            t = self._rope_tab = (emb.cos().to(dtype), emb.sin().to(dtype))
+        return t
+
+    def _fused_prologue(self, hidden_states: torch.Tensor, cache: "PreallocatedKVCache"):
+        """q/k RMSNorm + RoPE + the append of k/v to the preallocated cache in one
+        kernel (ops.qk_norm_rope_append) after one fused projection GEMM, in place
+        of q_norm / k_norm / apply_rotary_pos_emb / cache.update
+        (modeling_sparse_qwen3.py:211-231). Returns q [B, Hq, T, D] and the cache's
+        k / v views [B, Hkv, length, D]."""
+        B, T, _ = hidden_states.shape
+        H, Hkv, D = self.num_heads, self.num_key_value_heads, self.head_dim
+        cl = cache.layers[self.layer_idx]
+        if not cl.is_initialized:
+            z = torch.empty(B, Hkv, 0, D, dtype=hidden_states.dtype, device=hidden_states.device)
+            cl.lazy_initialization(z, z)
+        if cl.length + T > cl.capacity:
+            raise RuntimeError(f"KV cache capacity {cl.capacity} exceeded")
+        qkv = (hidden_states @ self._fused_qkv_weight().t()).view(B, T, H + 2 * Hkv, D)
+        cos, sin = self._rope_tables(cl.capacity, qkv.device, qkv.dtype)
+        q = _ops.qk_norm_rope_append(qkv, self.q_norm.weight, self.k_norm.weight, cos, sin, cl.k_buf, cl.v_buf,
+                                     Hq=H, Hkv=Hkv, pos=cl.length, eps=self.q_norm.variance_epsilon)
+        cl.length += T
+        cl.keys, cl.values = cl.k_buf[:, :, :cl.length], cl.v_buf[:, :, :cl.length]
+        return q, cl.keys, cl.values
+
     def forward(self, hidden_states: torch.Tensor, position_embeddings: tuple[torch.Tensor, torch.Tensor],
                 attention_mask: Optional[torch.Tensor] = None, past_key_values: Optional[Cache] = None, **kwargs):
         if kwargs.get("output_attentions", False):
             raise NotImplementedError("Sparse kernel path does not return attention weights.")
         input_shape = hidden_states.shape[:-1]
         hidden_shape = (*input_shape, -1, self.head_dim)
-        q = self.q_norm(self.q_proj(hidden_states).view(hidden_shape)).transpose(1, 2)
-        k = self.k_norm(self.k_proj(hidden_states).view(hidden_shape)).transpose(1, 2)
-        v = self.v_proj(hidden_states).view(hidden_shape).transpose(1, 2)
-        cos, sin = position_embeddings
-        q, k = apply_rotary_pos_emb(q, k, cos, sin)
-        if past_key_values is not None:
-            k, v = past_key_values.update(k, v, self.layer_idx)
+        if self._fusable and isinstance(past_key_values, PreallocatedKVCache) and \
+                hidden_states.dtype == torch.bfloat16 and hidden_states.is_cuda:
+            q, k, v = self._fused_prologue(hidden_states, past_key_values)
+        else:
+            q = self.q_norm(self.q_proj(hidden_states).view(hidden_shape)).transpose(1, 2)
+            k = self.k_norm(self.k_proj(hidden_states).view(hidden_shape)).transpose(1, 2)
+            v = self.v_proj(hidden_states).view(hidden_shape).transpose(1, 2)
+            cos, sin = position_embeddings
+            q, k = apply_rotary_pos_emb(q, k, cos, sin)
+            if past_key_values is not None:
+                k, v = past_key_values.update(k, v, self.layer_idx)
         if self.dense and self.dense_impl == "sdpa" and q.shape[2] in (1, k.shape[2]):
             # (SDPA aligns its causal mask top-left, so chunked prefill, 1 < T_q < T_k,
             # stays on the cuda_sm100 kernel, whose mask is bottom-right aligned.)
@@ -308,8 +377,69 @@ class PreallocatedKVCache(Cache):
         super().__init__(layers=[PreallocatedLayer(capacity) for _ in range(num_layers)])
 
 
+def hf_model_over_tp(runner) -> tuple[Qwen3ForCausalLM, "PreallocatedKVCache"]:
+    """The reference's model API over a one-rank ``tp.Qwen3TPRunner``'s state: an
+    HF ``Qwen3ForCausalLM`` whose attention layers are ``Qwen3SparseKernelAttention``
+    (the runner's BigBird layout in its sparse layers, dense elsewhere) with every
+    parameter a view of the runner's weights (no copy), and a
+    ``PreallocatedKVCache`` over the runner's KV cache at ``runner.length``. Decoding
+    through it runs the hook path (HF modules, ``pattern.build`` per call) from
+    the same prefilled cache."""
+    from transformers.models.qwen3.modeling_qwen3 import Qwen3RotaryEmbedding
+
+    if runner.w.world != 1:
+        raise ValueError("needs a one-rank runner")
+    A, w = runner.A, runner.w
+    D, H, Hkv = A.head_dim, A.heads, A.kv_heads
+    cfg = Qwen3Config(vocab_size=A.vocab, hidden_size=A.hidden, intermediate_size=A.intermediate,
+                      num_hidden_layers=A.layers, num_attention_heads=H, num_key_value_heads=Hkv, head_dim=D,
+                      rms_norm_eps=A.eps, rope_theta=A.rope_theta, tie_word_embeddings=A.tie_embeddings,
+                      max_position_embeddings=runner.capacity)
+    cfg._attn_implementation = register_attention_implementation()
+    cfg.sparse_attention_pattern = "bigbird"
+    cfg.sparse_attention_layer_layouts = [[list(runner.layout)] if li in runner.sparse else None
+                                          for li in range(A.layers)]
+    cfg.sparse_attention_dense_impl = "cuda_sm100"
+    with torch.device("meta"):
+        model = Qwen3ForCausalLM(cfg)
+        for li, layer in enumerate(model.model.layers):
+            layer.self_attn = Qwen3SparseKernelAttention(cfg, li)
+
+    def put(mod, t):
+        mod._parameters["weight"] = nn.Parameter(t, requires_grad=False)
+
+    put(model.model.embed_tokens, w.embed)
+    put(model.model.norm, w.final_norm)
+    put(model.lm_head, w.lm_head)
+    for layer, L in zip(model.model.layers, w.layers):
+        a, m = layer.self_attn, layer.mlp
+        put(a.q_proj, L["qkv"][: H * D])
+        put(a.k_proj, L["qkv"][H * D:(H + Hkv) * D])
+        put(a.v_proj, L["qkv"][(H + Hkv) * D:])
+        put(a.o_proj, L["o"])
+        put(a.q_norm, L["qn"])
+        put(a.k_norm, L["kn"])
+        inter = L["gu"].shape[0] // 2
+        put(m.gate_proj, L["gu"][:inter])
+        put(m.up_proj, L["gu"][inter:])
+        put(m.down_proj, L["down"])
+        put(layer.input_layernorm, L["ln1"])
+        put(layer.post_attention_layernorm, L["ln2"])
+    dev = w.embed.device
+    model.model.rotary_emb = Qwen3RotaryEmbedding(cfg, device=dev)
+    model.eval()
+    cache = PreallocatedKVCache(A.layers, runner.capacity)
+    for li, cl in enumerate(cache.layers):
+        cl.dtype, cl.device = w.embed.dtype, dev
+        cl.k_buf, cl.v_buf = runner.k_cache[li], runner.v_cache[li]
+        cl.length = runner.length
+        cl.keys, cl.values = cl.k_buf[:, :, :cl.length], cl.v_buf[:, :, :cl.length]
+        cl.is_initialized = True
+    return model, cache
+
+
 __all__ = [
     "Qwen3SparseKernelAttention", "replace_qwen3_attention_with_sparse", "build_sparse_attention_from_dense",
     "Qwen3SparseKernelForCausalLM", "PreallocatedKVCache", "PreallocatedLayer", "build_layer_block_experiments",
-    "normalize_group_sparsities", "normalize_layer_group_sparsities",
+    "normalize_group_sparsities", "normalize_layer_group_sparsities", "hf_model_over_tp",
 ]

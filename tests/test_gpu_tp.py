@@ -136,3 +136,30 @@ def test_graph_decode_matches_eager_across_block_boundary():
     assert graph.length == eager.length == T + steps
     assert all(bool((p == 7).all()) for p in probes)
     assert _capi.device_error() == 0
+
+
+def test_hook_model_decodes_like_the_runner():
+    """hf_model_over_tp: the HF model with Qwen3SparseKernelAttention over the same
+    weights and a copy of the same prefilled cache decodes the runner's logits
+    (the two differ only in where RMSNorm / RoPE round: HF modules vs the fused
+    kernel)."""
+    from sparseattentioninfer_b200.qwen3 import hf_model_over_tp
+    A = tp.Qwen3Arch(hidden=512, layers=2, heads=32, kv_heads=8, head_dim=128, intermediate=1024, vocab=2000)
+    w = tp.Qwen3TPWeights(A, 0, 1, seed=11, device=DEV)
+    T, steps = 1000, 6
+    tok = torch.randint(0, A.vocab, (2, T), generator=torch.Generator().manual_seed(5)).to(DEV)
+    feed = torch.randint(0, A.vocab, (steps, 2, 1), generator=torch.Generator().manual_seed(6)).to(DEV)
+    r1 = tp.Qwen3TPRunner(w, 2, T + steps, (64, 2, 4, 2), sparse_layers=[0])
+    r2 = tp.Qwen3TPRunner(w, 2, T + steps, (64, 2, 4, 2), sparse_layers=[0])
+    r1.prefill(tok, chunk=256)
+    r2.prefill(tok, chunk=256)
+    model, cache = hf_model_over_tp(r2)
+    got, ref = [], []
+    with torch.no_grad():
+        for i in range(steps):
+            ref.append(r1.step(feed[i], return_logits=True)[1].float().cpu())
+            got.append(model(input_ids=feed[i], past_key_values=cache, use_cache=True).logits[:, -1].float().cpu())
+    torch.cuda.synchronize()
+    _compare(got, ref, "hook vs runner")
+    assert all(cl.length == T + steps for cl in cache.layers)
+    assert _capi.device_error() == 0
