@@ -409,7 +409,7 @@ def time_gqa_layer(device, rank: int, world: int) -> dict:
 
 
 def time_tp_model(device, rank: int, world: int, *, prompt=65536, steps=512, batch=8, chunk=4096,
-                  seed=0, use_nvlink_ar=True) -> dict:
+                  seed=0, use_nvlink_ar=True, overlap=True) -> dict:
     """Config 5: random-init Qwen3-8B architecture (hidden 4096, 36 layers, 32/8
     heads, head_dim 128, SwiGLU 12288, vocab 151936, weights N(0, 0.02)) in bf16,
     tensor-parallel over the KV groups (sparseattentioninfer_b200.tp; NCCL
@@ -424,7 +424,7 @@ def time_tp_model(device, rank: int, world: int, *, prompt=65536, steps=512, bat
     if world > 1 and use_nvlink_ar:
         from sparseattentioninfer_b200.comm import NvlinkAllReduce
         comm = NvlinkAllReduce(batch * tp.QWEN3_8B.hidden * 2, device=device)  # decode messages
-    runner = tp.Qwen3TPRunner(w, batch, prompt + steps + 64, (128, 2, 4, 3), comm=comm)
+    runner = tp.Qwen3TPRunner(w, batch, prompt + steps + 64, (128, 2, 4, 3), comm=comm, overlap_prefill=overlap)
     tok = torch.randint(0, tp.QWEN3_8B.vocab, (batch, prompt), generator=torch.Generator().manual_seed(5))
     tok = tok.to(device)
 
@@ -472,6 +472,7 @@ def time_tp_model(device, rank: int, world: int, *, prompt=65536, steps=512, bat
            "ttft_s": ttft, "prefill_tok_s": batch * prompt / ttft, "decode_tok_s": batch * steps / dec,
            "decode_ms_per_step": dec / steps * 1e3, "decode": "CUDA graph per step (captured once)",
            "decode_eager_tok_s": batch * eager_steps / dec_eager, "n_gpus": world,
+           "prefill_overlap": bool(overlap and world > 1),
            "collective": ("none" if world == 1 else
                           "decode: fused NVLink peer-memory all-reduce + residual add + RMSNorm (one kernel) after "
                           "o_proj and down_proj; prefill: NCCL all-reduce" if comm is not None else
@@ -751,7 +752,8 @@ def run_ours(args) -> None:
     tp_model = None
     if args.tp_model == "on":
         try:
-            tp_model = time_tp_model(device, rank, world, prompt=args.tp_prompt, steps=args.tp_steps)
+            tp_model = time_tp_model(device, rank, world, prompt=args.tp_prompt, steps=args.tp_steps,
+                                     overlap=args.tp_overlap == "on")
         except Exception as e:  # noqa: BLE001
             tp_model = {"error": repr(e)[:300]}
 
@@ -848,6 +850,8 @@ def main() -> None:
                     help="also time the tensor-parallel Qwen3-8B-shaped model (config 5) on all ranks")
     ap.add_argument("--tp-prompt", type=int, default=65536)
     ap.add_argument("--tp-steps", type=int, default=512)
+    ap.add_argument("--tp-overlap", choices=["on", "off"], default="on",
+                    help="overlap the prefill all-reduces with compute (two batch halves)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

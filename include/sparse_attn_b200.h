@@ -162,6 +162,12 @@ SA_API int sa_kvlist_pairs(const int32_t* kv_block_list, int32_t H, int32_t NQB,
  * in [16, 512]. pairs [Hq, pairs_stride] / offsets [Hq, NQB+1] int32 device
  * arrays, NQB = ceil(T_q / block_size).
  * Uses tcgen05 MMAs with TMEM accumulators and TMA tile loads; persistent grid.
+ * Tiles are handed out by a counter in one of 64 library-owned scheduler slots;
+ * each call takes the next slot (round robin per device) and its last CTA
+ * re-arms it. So at most 64 prefill launches may be in flight at once on a
+ * device, and a launch recorded in a CUDA graph keeps its slot: replays of it
+ * must not overlap each other, nor run while 64 or more other prefill launches
+ * are issued and still in flight.
  * ------------------------------------------------------------------------- */
 typedef struct {
   const void* q;
@@ -318,7 +324,11 @@ SA_API int sa_topk_softmax_pv(const sa_topk_args* args, sa_stream_t stream);
  *   out = x * rsqrt(mean(x^2) + eps) * weight.
  * Consecutive calls must alternate between the two slots. Waits for peers are
  * bounded (2 s); on expiry the device error word reads SA_DEV_ERR_TIMEOUT and x
- * is left unchanged. Plain loads/stores to peer memory only (no multicast).
+ * is left unchanged. A timed-out call has already advanced this rank's epochs
+ * and published its flags while the missing peer has not, so before the next
+ * call every rank must zero its epoch counters and its flag region (all ranks
+ * together, between barriers: NvlinkAllReduce.reset() in Python). Plain
+ * loads/stores to peer memory only (no multicast).
  * ------------------------------------------------------------------------- */
 #define SA_AR_MAX_WORLD 8
 typedef struct sa_ar_peers {

@@ -118,6 +118,21 @@ class NvlinkAllReduce:
             x2.shape[0], n, x2.stride(0), o2.stride(0), float(eps), torch.cuda.current_stream(x.device).cuda_stream))
         return out
 
+    def reset(self) -> None:
+        """Re-arm after a timed-out call (the device error word read SA_DEV_ERR_TIMEOUT).
+        A timeout leaves this rank's epochs advanced and its flags published while
+        a peer's are not, so later calls would pair different epochs. All ranks
+        call reset() together: each zeroes its epoch counters and its flag region,
+        between two barriers, before the next call."""
+        import torch.distributed as dist
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        with torch.cuda.device(self.device):
+            self.epoch.zero_()
+            _as_tensor(self._own[1], (self.max_ctas * _MAX_WORLD,), torch.int32, self.device).zero_()
+            torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+
     def close(self) -> None:
         """Unmap the peers' regions and free this rank's (all ranks call it together)."""
         import torch.distributed as dist

@@ -139,7 +139,8 @@ class Qwen3TPRunner:
 
     def __init__(self, weights: Qwen3TPWeights, batch: int, capacity: int, layout: Sequence[int],
                  *, sparse_layers: Optional[Sequence[int]] = None, group=None, n_split: Optional[int] = None,
-                 kernels=None, comm=None, dense_impl: str = "cuda_sm100"):
+                 kernels=None, comm=None, dense_impl: str = "cuda_sm100",
+                 overlap_prefill: bool = True):
         self.w = weights
         # dense layers: "cuda_sm100" (this package's kernels over a dense CSR;
         # graph-capturable) or "sdpa" (PyTorch SDPA, the library comparator; eager
@@ -175,6 +176,8 @@ class Qwen3TPRunner:
         self.length = 0
         self._csr = {}
         self._ws = None
+        self._comm_stream = None
+        self.overlap_prefill = overlap_prefill
         self._graph = None
         self._g_csr = {}
 
@@ -249,6 +252,78 @@ class Qwen3TPRunner:
             h = self._layer(x, h, li, T=T, pos=pos, pos_dev=pos_dev, attend=attend, next_norm=nxt)
         return h[:, -1]
 
+    def _half_stream(self, tok: torch.Tensor, b0: int, b1: int, pos: int, attend, out: list):
+        """The decoder layers for batch rows [b0, b1) as a generator that yields each
+        row-parallel partial sum (o_proj, then down_proj, per layer) for the caller
+        to all-reduce in place before resuming it; leaves the last position's
+        final-norm hidden state in ``out``."""
+        ops, A, w = self.ops, self.A, self.w
+        D, hq, hkv = A.head_dim, w.hq, w.hkv
+        B, T = b1 - b0, tok.shape[1]
+        x = F.embedding(tok[b0:b1], w.embed)
+        h = ops.add_rms_norm(x, None, w.layers[0]["ln1"], A.eps)
+        for li in range(A.layers):
+            L = w.layers[li]
+            qkv = (h @ L["qkv"].t()).view(B, T, hq + 2 * hkv, D)
+            q = ops.qk_norm_rope_append(qkv, L["qn"], L["kn"], self.cos, self.sin, self.k_cache[li][b0:b1],
+                                        self.v_cache[li][b0:b1], Hq=hq, Hkv=hkv, pos=pos, eps=A.eps)
+            y = attend(li, q, b0, b1) @ L["o"].t()
+            yield y
+            h = ops.add_rms_norm(x, y, L["ln2"], A.eps)
+            y = ops.silu_mul(h @ L["gu"].t()) @ L["down"].t()
+            yield y
+            nxt = w.layers[li + 1]["ln1"] if li + 1 < A.layers else w.final_norm
+            h = ops.add_rms_norm(x, y, nxt, A.eps)
+        out.append(h[:, -1])
+
+    def _forward_overlapped(self, tok: torch.Tensor, pos: int, attend) -> torch.Tensor:
+        """_forward with the NCCL all-reduces hidden behind compute: the batch is
+        split in two halves whose layers are interleaved on the compute stream,
+        while a second stream all-reduces one half's partial sum as the other half
+        computes (the halves share nothing until the logits). Same arithmetic
+        per row as _forward."""
+        B = tok.shape[0]
+        halves = [(0, B // 2), (B // 2, B)]
+        outs = [[], []]
+        gens = [self._half_stream(tok, b0, b1, pos, attend, outs[i]) for i, (b0, b1) in enumerate(halves)]
+        cuda = tok.is_cuda  # on the host (gloo ranks) the same interleaving runs in order
+        comp = torch.cuda.current_stream(tok.device) if cuda else None
+        comm = self._comm_stream
+        if cuda and (comm is None or comm.device != tok.device):
+            comm = self._comm_stream = torch.cuda.Stream(device=tok.device)
+        ev_ar = [None, None]
+
+        def launch(i, y):
+            if not cuda:
+                all_reduce_(y, self.group)
+                return
+            ev = torch.cuda.Event()
+            ev.record(comp)
+            with torch.cuda.stream(comm):
+                comm.wait_event(ev)
+                all_reduce_(y, self.group)
+                y.record_stream(comm)
+                done = torch.cuda.Event()
+                done.record(comm)
+            ev_ar[i] = done
+
+        active = [True, True]
+        for i in range(2):
+            launch(i, next(gens[i]))
+        while any(active):
+            for i in range(2):
+                if not active[i]:
+                    continue
+                if cuda:
+                    comp.wait_event(ev_ar[i])
+                try:
+                    y = gens[i].send(None)
+                except StopIteration:
+                    active[i] = False
+                    continue
+                launch(i, y)
+        return torch.cat([outs[0][0], outs[1][0]], 0)
+
     def _logits(self, h_last: torch.Tensor) -> torch.Tensor:
         return (h_last @ self.w.lm_head.t()).float()
 
@@ -276,15 +351,27 @@ class Qwen3TPRunner:
             att = torch.empty(B, C, hq, D, device=tokens.device, dtype=self.dtype)
             chunk_offs = {d: offs[:, qb0:qb1 + 1].contiguous() for d, (_, offs) in csr.items()}
 
-            def attend(li, q, c1=c1, att=att, chunk_offs=chunk_offs):
+            def attend(li, q, b0=0, b1=B, c1=c1, att=att, chunk_offs=chunk_offs):
                 dense = li not in self.sparse
-                ops.prefill_fwd(q, self.k_cache[li][:, :, :c1], self.v_cache[li][:, :, :c1], csr[dense][0],
-                                chunk_offs[dense], self.bs, out=att.transpose(1, 2))
-                return att.view(B, -1, hq * D)
+                a = att[b0:b1]
+                ops.prefill_fwd(q, self.k_cache[li][b0:b1, :, :c1], self.v_cache[li][b0:b1, :, :c1],
+                                csr[dense][0], chunk_offs[dense], self.bs, out=a.transpose(1, 2))
+                return a.view(b1 - b0, -1, hq * D)
 
-            h_last = self._forward(tokens[:, c0:c1], c0, None, attend)
+            if self._overlap_prefill(B):
+                h_last = self._forward_overlapped(tokens[:, c0:c1], c0, attend)
+            else:
+                h_last = self._forward(tokens[:, c0:c1], c0, None, attend)
         self.length = T
         return self._logits(h_last)
+
+    def _overlap_prefill(self, B: int) -> bool:
+        """Prefill all-reduces overlap compute (two batch halves) on more than one
+        rank with an even batch; ``overlap_prefill=False`` turns it off."""
+        if not self.overlap_prefill or B < 2 or B % 2:
+            return False
+        import torch.distributed as dist
+        return dist.is_available() and dist.is_initialized() and dist.get_world_size(self.group) > 1
 
     # -- decode ----------------------------------------------------------------
     def _n_split(self) -> int:

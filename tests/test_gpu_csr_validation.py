@@ -10,7 +10,7 @@ import pytest
 import torch
 
 import sparseattentioninfer_b200 as sa
-from sparseattentioninfer_b200 import _capi, ops
+from sparseattentioninfer_b200 import _capi, ops, workloads
 from sparseattentioninfer_b200.patterns import PatternMetadata
 
 pytestmark = pytest.mark.gpu
@@ -45,7 +45,7 @@ def test_invalid_csr_is_rejected(mutate, what):
 
 
 def test_backend_rejects_caller_csr_and_accepts_compiled():
-    q, k, v = sa.workloads.seeded_qkv(1, 1, H, H, T, T, D, device=DEV, dtype=torch.bfloat16)
+    q, k, v = workloads.seeded_qkv(1, 1, H, H, T, T, D, device=DEV, dtype=torch.bfloat16)
     pairs, offs = _good()
     be = sa.get_backend("cuda_sm100")
     md = PatternMetadata(kind="mask", block_size=BS, block_pairs=pairs, block_pair_offsets=offs)
