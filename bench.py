@@ -833,6 +833,30 @@ def run_ours(args) -> None:
         torch.distributed.destroy_process_group()
 
 
+def profile_case(which: str) -> None:
+    """Three launches of one kernel on its bench shape, nothing else: the command
+    the ncu summaries under profiles/ were captured from (`--profile-case`)."""
+    from sparseattentioninfer_b200 import BigBirdKeepRatioPattern, ops, workloads as wl
+    device = torch.device("cuda", 0)
+    if which == "decode":
+        Bd, Hq, Hkv, T = 32, 32, 8, 32768
+        q, k, v = wl.seeded_qkv(7, Bd, Hq, Hkv, 1, T, D, device=device, dtype=torch.bfloat16)
+        md = BigBirdKeepRatioPattern(layouts=[(64, 2, 4, 2)], n_heads=Hq).build(q, k)
+        ns = ops.default_n_split(q, k)
+        out = torch.empty_like(q)
+        for _ in range(3):
+            ops.decode_fwd(q, k, v, md.block_pairs, md.block_pair_offsets, 64, n_split=ns, out=out)
+        info = {"n_split": ns}
+    else:
+        q, k, v, md, _, _ = make_workload(0, 1, device)
+        out = torch.empty_like(q)
+        for _ in range(3):
+            ops.prefill_fwd(q, k, v, md.block_pairs, md.block_pair_offsets, BS, out=out)
+        info = {}
+    torch.cuda.synchronize()
+    emit({"profile_case": which, **info})
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -852,7 +876,12 @@ def main() -> None:
     ap.add_argument("--tp-steps", type=int, default=512)
     ap.add_argument("--tp-overlap", choices=["on", "off"], default="on",
                     help="overlap the prefill all-reduces with compute (two batch halves)")
+    ap.add_argument("--profile-case", choices=["prefill", "decode"], default=None,
+                    help="only run three launches of one kernel (for ncu captures) and exit")
     args = ap.parse_args()
+    if args.profile_case:
+        profile_case(args.profile_case)
+        return
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
