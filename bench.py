@@ -753,7 +753,8 @@ def run_ours(args) -> None:
     if args.tp_model == "on":
         try:
             tp_model = time_tp_model(device, rank, world, prompt=args.tp_prompt, steps=args.tp_steps,
-                                     overlap=args.tp_overlap == "on")
+                                     overlap=args.tp_overlap == "on", use_nvlink_ar=args.tp_ar == "fused",
+                                     chunk=args.tp_chunk)
         except Exception as e:  # noqa: BLE001
             tp_model = {"error": repr(e)[:300]}
 
@@ -874,6 +875,9 @@ def main() -> None:
                     help="also time the tensor-parallel Qwen3-8B-shaped model (config 5) on all ranks")
     ap.add_argument("--tp-prompt", type=int, default=65536)
     ap.add_argument("--tp-steps", type=int, default=512)
+    ap.add_argument("--tp-chunk", type=int, default=8192, help="prefill chunk (tokens per row)")
+    ap.add_argument("--tp-ar", choices=["fused", "nccl"], default="fused",
+                    help="decode all-reduce: fused NVLink kernel or NCCL")
     ap.add_argument("--tp-overlap", choices=["on", "off"], default="on",
                     help="overlap the prefill all-reduces with compute (two batch halves)")
     ap.add_argument("--profile-case", choices=["prefill", "decode"], default=None,
