@@ -25,21 +25,6 @@ class AttentionBackend(ABC):
     """sparse_attentions/attention/base.py:9-40."""
 
     @abstractmethod
-    def _validate(self, pairs, offsets, T_q: int, T_k: int, bs: int) -> None:
-        """A CSR from outside this package (e.g. the reference's own pattern
-        objects) is validated once per tensor pair and contents (sa_validate_csr;
-        the tensors are held by weak reference, their in-place version counters
-        detect changes); a violation raises SaError (SA_ERR_CSR)."""
-        key = (id(pairs), id(offsets), T_q, T_k, bs)
-        hit = self._validated.get(key)
-        if hit is not None and hit[0]() is pairs and hit[1]() is offsets and \
-                hit[2] == (pairs._version, offsets._version):
-            return
-        _ops.validate_csr(pairs, offsets, T_q, T_k, bs)
-        self._validated[key] = (weakref.ref(pairs), weakref.ref(offsets), (pairs._version, offsets._version))
-        while len(self._validated) > 64:
-            self._validated.pop(next(iter(self._validated)))
-
     def forward(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, pattern: PatternMetadata) -> torch.Tensor:
         ...
 

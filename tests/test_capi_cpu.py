@@ -112,3 +112,10 @@ def test_validate_csr_host_arguments():
     lib = _capi.load()
     assert lib.sa_validate_csr(None, None, 1, 1, 1, 1, None, None) == _capi.SA_ERR_INVALID
     assert lib.sa_validate_csr(1 << 20, 1 << 20, 0, 1, 1, 1, 1 << 20, None) == _capi.SA_ERR_INVALID
+
+
+def test_attention_backend_is_abstract():
+    import sparseattentioninfer_b200 as sa
+    with pytest.raises(TypeError):
+        sa.AttentionBackend()
+    assert "forward" in sa.AttentionBackend.__abstractmethods__
