@@ -62,6 +62,7 @@ struct PrefillParams {
   const int32_t* offsets;
   int32_t pairs_stride;
   int32_t B, Hq, Hkv, T_q, T_k, bs, nqb, nqt, group;
+  int32_t qt_major;  // tile order: 0 head-major, 1 query-tile-major (see tile_coord)
   float scale_log2;
   int32_t* err;
   uint32_t* sched;  // {next tile, CTAs finished} of this launch's scheduler slot
@@ -185,11 +186,15 @@ struct TileCoord {
 };
 
 // Head-major order (consecutive tiles share one (b, head), so its K/V stays in
-// L2), heaviest (last) query tile of each head first.
+// L2), heaviest (last) query tile of each head first. When the launch's whole
+// K/V fits in L2 (qt_major), the order is query-tile-major instead: the
+// heaviest tiles of every head first, the lightest last, which shortens the
+// tail of small launches (a rank's shard of a layer).
 template <int N>
 __device__ __forceinline__ TileCoord tile_coord(const PrefillParams& p, int t) {
-  const int bh = t / p.nqt;
-  const int qt = p.nqt - 1 - t % p.nqt;
+  const int nbh = p.B * p.Hq;
+  const int bh = p.qt_major ? t % nbh : t / p.nqt;
+  const int qt = p.nqt - 1 - (p.qt_major ? t / nbh : t % p.nqt);
   TileCoord c;
   c.b = bh / p.Hq;
   c.h = bh % p.Hq;
@@ -835,6 +840,16 @@ extern "C" int sa_prefill_fwd(const sa_attn_args* a, sa_stream_t stream_) {
   prm.nqb = (a->T_q + bs - 1) / bs;
   prm.nqt = (a->T_q + kTileM - 1) / kTileM;
   prm.group = a->Hq / a->Hkv;
+  {
+    // Query-tile-major order when K and V of the whole launch stay in L2
+    // (126 MB; the bound leaves room for the streamed Q and output). Measured on
+    // config-2 shards (B=4, S=8192, bs 128): 4 heads (67 MB of K/V) 107 -> 88 us,
+    // 8 heads (134 MB) no change, 16 and 32 heads slower in this order.
+    const int64_t kv_bytes = 2ll * a->B * a->Hkv * a->T_k * a->D * 2;
+    int order = kv_bytes <= (96ll << 20) ? 1 : 0;
+    if (const char* e = getenv("SA_PREFILL_ORDER")) order = atoi(e) == 2 ? 1 : atoi(e) == 1 ? 0 : order;
+    prm.qt_major = order;
+  }
   prm.scale_log2 = a->scale * 1.4426950408889634f;
   prm.err = sa_device_error_ptr();
   if ((rc = sched_slot(&prm.sched))) return rc;
