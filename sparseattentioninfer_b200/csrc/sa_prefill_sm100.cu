@@ -62,7 +62,7 @@ struct PrefillParams {
   const int32_t* offsets;
   int32_t pairs_stride;
   int32_t B, Hq, Hkv, T_q, T_k, bs, nqb, nqt, group;
-  int32_t qt_major;  // tile order: 0 head-major, 1 query-tile-major (see tile_coord)
+  int32_t qt_tail;   // (b, head) pairs at the end visited query-tile-major (see tile_coord)
   float scale_log2;
   int32_t* err;
   uint32_t* sched;  // {next tile, CTAs finished} of this launch's scheduler slot
@@ -186,15 +186,24 @@ struct TileCoord {
 };
 
 // Head-major order (consecutive tiles share one (b, head), so its K/V stays in
-// L2), heaviest (last) query tile of each head first. When the launch's whole
-// K/V fits in L2 (qt_major), the order is query-tile-major instead: the
-// heaviest tiles of every head first, the lightest last, which shortens the
-// tail of small launches (a rank's shard of a layer).
+// L2), heaviest (last) query tile of each head first — except for the last
+// qt_tail (b, head) pairs, which are visited query-tile-major: the heaviest
+// tiles of all of them first, the lightest last. Otherwise the heavy tiles of
+// the last heads would start when the other CTAs are running dry and set the
+// launch's tail. Their K/V (qt_tail heads) is sized to stay in L2.
 template <int N>
 __device__ __forceinline__ TileCoord tile_coord(const PrefillParams& p, int t) {
   const int nbh = p.B * p.Hq;
-  const int bh = p.qt_major ? t % nbh : t / p.nqt;
-  const int qt = p.nqt - 1 - (p.qt_major ? t / nbh : t % p.nqt);
+  const int head_tiles = (nbh - p.qt_tail) * p.nqt;
+  int bh, qt;
+  if (t < head_tiles) {
+    bh = t / p.nqt;
+    qt = p.nqt - 1 - t % p.nqt;
+  } else {
+    const int u = t - head_tiles;
+    bh = nbh - p.qt_tail + u % p.qt_tail;
+    qt = p.nqt - 1 - u / p.qt_tail;
+  }
   TileCoord c;
   c.b = bh / p.Hq;
   c.h = bh % p.Hq;
@@ -840,16 +849,7 @@ extern "C" int sa_prefill_fwd(const sa_attn_args* a, sa_stream_t stream_) {
   prm.nqb = (a->T_q + bs - 1) / bs;
   prm.nqt = (a->T_q + kTileM - 1) / kTileM;
   prm.group = a->Hq / a->Hkv;
-  {
-    // Query-tile-major order when K and V of the whole launch stay in L2
-    // (126 MB; the bound leaves room for the streamed Q and output). Measured on
-    // config-2 shards (B=4, S=8192, bs 128): 4 heads (67 MB of K/V) 107 -> 88 us,
-    // 8 heads (134 MB) no change, 16 and 32 heads slower in this order.
-    const int64_t kv_bytes = 2ll * a->B * a->Hkv * a->T_k * a->D * 2;
-    int order = kv_bytes <= (96ll << 20) ? 1 : 0;
-    if (const char* e = getenv("SA_PREFILL_ORDER")) order = atoi(e) == 2 ? 1 : atoi(e) == 1 ? 0 : order;
-    prm.qt_major = order;
-  }
+  const int qt_tail_env = getenv("SA_PREFILL_TAIL") ? atoi(getenv("SA_PREFILL_TAIL")) : -1;
   prm.scale_log2 = a->scale * 1.4426950408889634f;
   prm.err = sa_device_error_ptr();
   if ((rc = sched_slot(&prm.sched))) return rc;
@@ -857,6 +857,17 @@ extern "C" int sa_prefill_fwd(const sa_attn_args* a, sa_stream_t stream_) {
   if (ntiles > 0x7fffffff) return sa_fail(SA_ERR_INVALID, "too many tiles");
   int sms = a->num_sms > 0 ? a->num_sms : sa_num_sms();
   if (sms <= 0) return sa_fail(SA_ERR_CUDA, "cannot query SM count");
+  {
+    // Tail visited query-tile-major: enough (b, head) pairs for two tiles per
+    // resident CTA, all of them when the launch's K/V stays in L2 (<= 96 MB;
+    // measured on config-2 shards: 4 heads 107 -> 86 us).
+    const int nbh = a->B * a->Hq;
+    const int64_t kv_bytes = 2ll * a->B * a->Hkv * a->T_k * a->D * 2;
+    int tail = (int)((2ll * 2 * sms + prm.nqt - 1) / prm.nqt);
+    if (kv_bytes <= (96ll << 20)) tail = nbh;
+    if (qt_tail_env >= 0) tail = qt_tail_env;
+    prm.qt_tail = tail < 1 ? 1 : (tail > nbh ? nbh : tail);
+  }
   // Chunk size: 64 keys with two CTAs per SM (default; their softmax
   // warpgroups interleave on the tensor core), or 128 keys with one CTA per SM
   // (SA_PREFILL_CHUNK=128).
