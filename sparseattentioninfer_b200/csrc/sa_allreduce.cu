@@ -8,9 +8,12 @@
 //      (this CTA, this rank) with a system-scope release, and waits (bounded)
 //      until its own flag words from every rank reach that epoch (acquire);
 //   2. reads y_0 .. y_{N-1} for its rows straight from the peers' memory
-//      (plain loads over NVLink, not cached in L1), sums them in fp32 in rank
-//      order — the same order on every rank, so all ranks hold identical
-//      residual streams — and does x = bf16(x + sum), out = RMSNorm(x) * w.
+//      (plain loads over NVLink, not cached in L1; every peer's 16 bytes are
+//      requested before any is summed, so a thread waits for one NVLink round
+//      trip, not one per peer), sums them in fp32 in rank order — the same
+//      order on every rank, so all ranks hold identical residual streams —
+//      and does x = bf16(x + sum), out = RMSNorm(x) * w. 512 threads cover a
+//      4096-wide row in one pass.
 // Calls alternate between two slots (o_proj, down_proj, o_proj, ...): a rank
 // can only overwrite slot s after every peer entered the next call, i.e.
 // finished reading s, so no exit barrier is needed. Epochs only grow, a peer
@@ -24,7 +27,7 @@
 namespace sa {
 
 constexpr int kArMaxWorld = SA_AR_MAX_WORLD;
-constexpr int kArThreads = 256;
+constexpr int kArThreads = 512;
 
 struct ArParams {
   const __nv_bfloat16* data[kArMaxWorld];  // every rank's y for this call (slot already applied)
@@ -86,14 +89,20 @@ __global__ void __launch_bounds__(kArThreads) ar_add_rms_norm_kernel(const ArPar
       float acc[8];
 #pragma unroll
       for (int k = 0; k < 8; ++k) acc[k] = 0.f;
-      for (int q = 0; q < p.world; ++q) {
-        const uint4 v = __ldcv(reinterpret_cast<const uint4*>(p.data[q] + r * p.n + i));
-        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
+      uint4 v[kArMaxWorld];
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const float2 f = __bfloat1622float2(h[k]);
-          acc[2 * k] += f.x;
-          acc[2 * k + 1] += f.y;
+      for (int q = 0; q < kArMaxWorld; ++q)
+        if (q < p.world) v[q] = __ldcv(reinterpret_cast<const uint4*>(p.data[q] + r * p.n + i));
+#pragma unroll
+      for (int q = 0; q < kArMaxWorld; ++q) {
+        if (q < p.world) {
+          const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v[q]);
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const float2 f = __bfloat1622float2(h[k]);
+            acc[2 * k] += f.x;
+            acc[2 * k + 1] += f.y;
+          }
         }
       }
       uint4 xv = *reinterpret_cast<const uint4*>(xr + i);
