@@ -285,6 +285,17 @@ SA_API int sa_add_rms_norm(void* x, const void* y, const void* weight, void* out
 SA_API int sa_silu_mul(const void* gate_up, void* out, int64_t rows, int32_t inter, int64_t gu_stride,
                        int64_t out_stride, sa_stream_t stream);
 
+/* Projection of M <= 8 tokens (decode), bf16 in and out, fp32 accumulation:
+ *   glu == 0: out[m, n] = sum_k x[m, k] * w[n, k],  n < N   (nn.Linear, no bias)
+ *   glu != 0: g, u = bf16 of the same sums over w rows n and N + n (the fused
+ *             [gate; up] weight), out[m, n] = bf16(silu(g) * u)  (Qwen3MLP
+ *             act_fn(gate_proj(x)) * up_proj(x) in one launch).
+ * K a multiple of 256, N a multiple of 16, x and w rows 16-byte aligned
+ * (element strides multiples of 8). Replaces the GEMM launches of the decoder
+ * layer at decode batch sizes, where the weight stream is the whole cost. */
+SA_API int sa_linear_m8(const void* x, int32_t M, int32_t K, int64_t x_stride, const void* w, int32_t N,
+                        int64_t w_stride, void* out, int64_t out_stride, int32_t glu, sa_stream_t stream);
+
 /* ---------------------------------------------------------------------------
  * Data-dependent top-k attention (TopKPattern; MaskedSdpaBackend's "topk" kind,
  * masked_sdpa.py:51-63), second half: given fp32 scores q.k^T.scale of a block

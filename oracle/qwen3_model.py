@@ -164,6 +164,20 @@ class CheckerKernels:
         return out
 
     @staticmethod
+    def linear_m8(x, weight, out=None, *, glu=False):
+        if glu:
+            n = weight.shape[0] // 2
+            g = (x.float() @ weight[:n].float().t()).to(x.dtype).float()
+            u = (x.float() @ weight[n:].float().t()).to(x.dtype).float()
+            o = (F.silu(g) * u).to(x.dtype)
+        else:
+            o = (x.float() @ weight.float().t()).to(x.dtype)
+        if out is None:
+            return o
+        out.copy_(o)
+        return out
+
+    @staticmethod
     def decode_fwd(q, k, v, block_pairs, block_pair_offsets, block_size, *, scale=None, n_split=None, out=None,
                    workspace=None):
         return CheckerKernels.prefill_fwd(q, k, v, block_pairs, block_pair_offsets, block_size, out=out)

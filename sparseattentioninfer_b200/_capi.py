@@ -33,6 +33,7 @@ EXPORTED = (
     "sa_qk_norm_rope_append",
     "sa_add_rms_norm",
     "sa_silu_mul",
+    "sa_linear_m8",
     "sa_topk_softmax_pv",
     "sa_ar_alloc",
     "sa_ar_free",
@@ -137,6 +138,7 @@ def load(path: str | os.PathLike | None = None) -> ctypes.CDLL:
     lib.sa_add_rms_norm.argtypes = [_c_p, _c_p, _c_p, _c_p, _c_i64, _c_i32, _c_i64, _c_i64, _c_i64, ctypes.c_float,
                                     _c_p]
     lib.sa_silu_mul.argtypes = [_c_p, _c_p, _c_i64, _c_i32, _c_i64, _c_i64, _c_p]
+    lib.sa_linear_m8.argtypes = [_c_p, _c_i32, _c_i32, _c_i64, _c_p, _c_i32, _c_i64, _c_p, _c_i64, _c_i32, _c_p]
     lib.sa_topk_softmax_pv.argtypes = [ctypes.POINTER(TopkArgs), _c_p]
     lib.sa_ar_alloc.argtypes = [ctypes.c_size_t, ctypes.POINTER(_c_p)]
     lib.sa_ar_free.argtypes = [_c_p]

@@ -10,6 +10,8 @@
 //   after each sub-block of the decoder layer).
 // * sa_silu_mul: the SwiGLU activation silu(gate) * up over the fused
 //   gate/up projection output (Qwen3MLP).
+// * sa_linear_m8: the decoder's projections for at most 8 tokens (decode),
+//   optionally with the SwiGLU activation fused into the gate/up projection.
 //
 // All arithmetic is fp32 with one bf16 rounding per stored value; the residual
 // stream is stored in bf16 after each add, as the model keeps it.
@@ -190,9 +192,147 @@ __global__ void __launch_bounds__(256) silu_mul_kernel(const __nv_bfloat16* __re
   }
 }
 
+// ---------------------------------------------------------------------------
+// Projections of M <= 8 tokens: out[m, n] = sum_k x[m, k] * W[n, k].
+//
+// At decode the weight matrix is the only large operand, so the kernel is a
+// weight stream: one CTA per 16 weight rows, its 8 warps splitting K. A thread
+// reads 16 contiguous bytes of two weight rows (g and g + 8) and of token row
+// g of x per 32-wide K chunk, with eight chunks (GLU: four, for twice the
+// rows) in flight before any math. The 32 K indices of a chunk are permuted
+// consistently in A and B, which the sum over K does not see, so those 16-byte
+// loads are exactly the mma.sync m16n8k16 fragments: weight rows are the
+// M = 16 side, the 8 tokens the N = 8 side (tokens >= M read zeros). Warps
+// are summed in a fixed order through shared memory (deterministic). With
+// GLU the CTA also streams the matching up-projection rows (W rows N + n) and
+// writes bf16(silu(g) * u) from the bf16-rounded g and u, the arithmetic of
+// silu_mul_kernel.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint4 ld_stream16(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
+__device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                          uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+constexpr int kLinWarps = 8;
+
+template <bool GLU>
+__global__ void __launch_bounds__(32 * kLinWarps) linear_m8_kernel(const __nv_bfloat16* __restrict__ x, int M, int K,
+                                                                   int64_t xs, const __nv_bfloat16* __restrict__ W,
+                                                                   int64_t ws, int N, __nv_bfloat16* out,
+                                                                   int64_t os) {
+  constexpr int NT = GLU ? 2 : 1;  // weight tiles per CTA (gate, up)
+  constexpr int U = GLU ? 4 : 8;   // K chunks in flight per thread
+  __shared__ float red[NT][kLinWarps][16][9];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
+  const int n0 = blockIdx.x * 16;
+  const int kw = K / kLinWarps;
+  const int nch = kw / 32;
+  const int64_t koff = (int64_t)warp * kw + 8 * c;
+  const __nv_bfloat16* wr[NT][2];
+#pragma unroll
+  for (int t = 0; t < NT; ++t) {
+    wr[t][0] = W + (int64_t)(n0 + t * N + g) * ws + koff;
+    wr[t][1] = wr[t][0] + 8 * ws;
+  }
+  const bool xrow = g < M;
+  const __nv_bfloat16* xp = x + (int64_t)(xrow ? g : 0) * xs + koff;
+  float acc[NT][4];
+#pragma unroll
+  for (int t = 0; t < NT; ++t)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) acc[t][i] = 0.f;
+  for (int c0 = 0; c0 < nch; c0 += U) {
+    uint4 wa[NT][U], wb[NT][U], xv[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      if (c0 + u < nch) {
+#pragma unroll
+        for (int t = 0; t < NT; ++t) {
+          wa[t][u] = ld_stream16(wr[t][0] + (c0 + u) * 32);
+          wb[t][u] = ld_stream16(wr[t][1] + (c0 + u) * 32);
+        }
+        xv[u] = xrow ? __ldg(reinterpret_cast<const uint4*>(xp + (c0 + u) * 32)) : make_uint4(0u, 0u, 0u, 0u);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      if (c0 + u < nch) {
+#pragma unroll
+        for (int t = 0; t < NT; ++t) {
+          mma_16816(acc[t], wa[t][u].x, wb[t][u].x, wa[t][u].y, wb[t][u].y, xv[u].x, xv[u].y);
+          mma_16816(acc[t], wa[t][u].z, wb[t][u].z, wa[t][u].w, wb[t][u].w, xv[u].z, xv[u].w);
+        }
+      }
+    }
+  }
+  // D fragment: acc[0..1] = rows g, tokens 2c, 2c+1; acc[2..3] = rows g + 8
+#pragma unroll
+  for (int t = 0; t < NT; ++t) {
+    red[t][warp][g][2 * c] = acc[t][0];
+    red[t][warp][g][2 * c + 1] = acc[t][1];
+    red[t][warp][g + 8][2 * c] = acc[t][2];
+    red[t][warp][g + 8][2 * c + 1] = acc[t][3];
+  }
+  __syncthreads();
+  if (threadIdx.x < 128) {
+    const int m = threadIdx.x >> 4, r = threadIdx.x & 15;
+    if (m < M) {
+      float sum[NT];
+#pragma unroll
+      for (int t = 0; t < NT; ++t) {
+        sum[t] = 0.f;
+#pragma unroll
+        for (int w = 0; w < kLinWarps; ++w) sum[t] += red[t][w][r][m];
+      }
+      float y;
+      if constexpr (GLU) {
+        const float gg = __bfloat162float(__float2bfloat16_rn(sum[0]));
+        const float uu = __bfloat162float(__float2bfloat16_rn(sum[1]));
+        y = gg / (1.f + __expf(-gg)) * uu;
+      } else {
+        y = sum[0];
+      }
+      out[(int64_t)m * os + n0 + r] = __float2bfloat16_rn(y);
+    }
+  }
+}
+
 }  // namespace sa
 
 using namespace sa;
+
+extern "C" int sa_linear_m8(const void* x, int32_t M, int32_t K, int64_t x_stride, const void* w, int32_t N,
+                            int64_t w_stride, void* out, int64_t out_stride, int32_t glu, sa_stream_t stream) {
+  if (!x || !w || !out) return sa_fail(SA_ERR_INVALID, "NULL pointer");
+  if (M < 1 || M > 8) return sa_fail(SA_ERR_UNSUPPORTED, "M=%d tokens (1..8)", M);
+  if (K <= 0 || K % (32 * kLinWarps) || N <= 0 || N % 16)
+    return sa_fail(SA_ERR_UNSUPPORTED, "K=%d (a multiple of %d), N=%d (a multiple of 16)", K, 32 * kLinWarps, N);
+  if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w)) & 15u || x_stride % 8 || w_stride % 8 ||
+      x_stride < K || w_stride < K || out_stride < N || (reinterpret_cast<uintptr_t>(out) & 1u))
+    return sa_fail(SA_ERR_INVALID, "x and W rows must start on 16-byte boundaries (strides %% 8 == 0, >= K)");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const auto* xb = static_cast<const __nv_bfloat16*>(x);
+  const auto* wb = static_cast<const __nv_bfloat16*>(w);
+  auto* ob = static_cast<__nv_bfloat16*>(out);
+  if (glu)
+    linear_m8_kernel<true><<<N / 16, 32 * kLinWarps, 0, s>>>(xb, M, K, x_stride, wb, w_stride, N, ob, out_stride);
+  else
+    linear_m8_kernel<false><<<N / 16, 32 * kLinWarps, 0, s>>>(xb, M, K, x_stride, wb, w_stride, N, ob, out_stride);
+  SA_CHECK_CUDA(cudaGetLastError());
+  return SA_OK;
+}
 
 static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 

@@ -379,6 +379,32 @@ def silu_mul(gate_up: torch.Tensor, out: torch.Tensor | None = None) -> torch.Te
     return out
 
 
+def linear_m8(x: torch.Tensor, weight: torch.Tensor, out: torch.Tensor | None = None, *,
+              glu: bool = False) -> torch.Tensor:
+    """x [..., K] (at most 8 rows) times weight [N, K]^T -> [..., N] (nn.Linear
+    without bias), one weight-streaming launch (sa_linear_m8). With ``glu`` the
+    weight is the fused [gate; up] matrix [2N, K] and the result is
+    silu(x W_gate^T) * (x W_up^T) [..., N] (Qwen3MLP's activation fused)."""
+    _require_cuda(x, weight)
+    if x.dtype != torch.bfloat16 or weight.dtype != torch.bfloat16:
+        raise TypeError("bf16 tensors expected")
+    K = x.shape[-1]
+    x2 = x.reshape(-1, K)
+    if x2.stride(-1) != 1 or weight.stride(-1) != 1:
+        raise ValueError("x and weight need unit stride in K")
+    N = weight.shape[0] // 2 if glu else weight.shape[0]
+    if out is None:
+        out = torch.empty(*x.shape[:-1], N, dtype=x.dtype, device=x.device)
+    o2 = out.view(-1, N)
+    if out.dtype != torch.bfloat16 or o2.stride(-1) != 1:
+        raise TypeError("out: bf16 with unit stride")
+    with torch.cuda.device(x.device):
+        _capi.check(_capi.load().sa_linear_m8(x2.data_ptr(), x2.shape[0], K, x2.stride(0), weight.data_ptr(), N,
+                                              weight.stride(0), o2.data_ptr(), o2.stride(0), int(bool(glu)),
+                                              _stream(x.device)))
+    return out
+
+
 
 def topk_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, top_k: int, *, scale: float | None = None,
                    max_score_bytes: int = 1 << 29) -> torch.Tensor:

@@ -140,8 +140,12 @@ class Qwen3TPRunner:
     def __init__(self, weights: Qwen3TPWeights, batch: int, capacity: int, layout: Sequence[int],
                  *, sparse_layers: Optional[Sequence[int]] = None, group=None, n_split: Optional[int] = None,
                  kernels=None, comm=None, dense_impl: str = "cuda_sm100",
-                 overlap_prefill: bool = True):
+                 overlap_prefill: bool = True, skinny_linear: bool = True):
         self.w = weights
+        # ``skinny_linear``: steps of at most 8 tokens (decode at batch <= 8) run
+        # their four projections through ops.linear_m8 (a weight-streaming
+        # kernel, SwiGLU fused into gate/up) instead of cuBLAS GEMMs.
+        self.skinny_linear = skinny_linear
         # dense layers: "cuda_sm100" (this package's kernels over a dense CSR;
         # graph-capturable) or "sdpa" (PyTorch SDPA, the library comparator; eager
         # decode only, its causal mask is top-left aligned so prefill stays on
@@ -225,20 +229,28 @@ class Qwen3TPRunner:
         L = w.layers[li]
         B = x.shape[0]
         D, hq, hkv = A.head_dim, w.hq, w.hkv
-        qkv = (h @ L["qkv"].t()).view(B, T, hq + 2 * hkv, D)
+        skinny = self.skinny_linear and B * T <= 8
+
+        def proj(inp, name, out=None, glu=False):
+            if skinny:
+                return ops.linear_m8(inp, L[name], out=out, glu=glu)
+            y = torch.matmul(inp, L[name].t(), out=out)
+            return ops.silu_mul(y) if glu else y
+
+        qkv = proj(h, "qkv").view(B, T, hq + 2 * hkv, D)
         q = ops.qk_norm_rope_append(qkv, L["qn"], L["kn"], self.cos, self.sin, self.k_cache[li], self.v_cache[li],
                                     Hq=hq, Hkv=hkv, pos=pos, pos_dev=pos_dev, eps=A.eps)
         att = attend(li, q)
         if self.comm is not None and self.comm.fits(B * T * A.hidden):
             shape = (B, T, A.hidden)
-            torch.matmul(att, L["o"].t(), out=self.comm.buffer(0, shape))
+            proj(att, "o", out=self.comm.buffer(0, shape))
             h = self.comm.add_rms_norm(0, x, L["ln2"], A.eps)
-            act = ops.silu_mul(h @ L["gu"].t())
-            torch.matmul(act, L["down"].t(), out=self.comm.buffer(1, shape))
+            act = proj(h, "gu", glu=True)
+            proj(act, "down", out=self.comm.buffer(1, shape))
             return self.comm.add_rms_norm(1, x, next_norm, A.eps)
-        h = ops.add_rms_norm(x, all_reduce_(att @ L["o"].t(), self.group), L["ln2"], A.eps)
-        act = ops.silu_mul(h @ L["gu"].t())
-        return ops.add_rms_norm(x, all_reduce_(act @ L["down"].t(), self.group), next_norm, A.eps)
+        h = ops.add_rms_norm(x, all_reduce_(proj(att, "o"), self.group), L["ln2"], A.eps)
+        act = proj(h, "gu", glu=True)
+        return ops.add_rms_norm(x, all_reduce_(proj(act, "down"), self.group), next_norm, A.eps)
 
     def _forward(self, tok: torch.Tensor, pos: int, pos_dev, attend) -> torch.Tensor:
         """All layers for tokens [B, T] at positions pos..; returns the final-norm

@@ -80,3 +80,50 @@ def test_silu_mul(rows, inter):
     f = gu.float()
     ref = torch.nn.functional.silu(f[:, :inter]) * f[:, inter:]
     torch.testing.assert_close(out.float(), ref, atol=2e-2, rtol=1e-2)
+
+
+@pytest.mark.parametrize("M,K,N,x_pad", [
+    (8, 4096, 768, 0), (8, 512, 4096, 0), (8, 1536, 4096, 0), (1, 256, 16, 0), (3, 4096, 6144, 8),
+    (5, 12288, 4096, 0), (8, 2560, 2560, 16), (7, 9728, 2560, 0),
+])
+def test_linear_m8(M, K, N, x_pad):
+    """sa_linear_m8 against an fp32 matmul of the same bf16 operands (one bf16
+    rounding of the output; K up to 12288 at N(0, 0.02) weights)."""
+    g = torch.Generator(device=DEV).manual_seed(K + N + M)
+    xs = torch.randn(M, K + x_pad, generator=g, device=DEV).to(torch.bfloat16)
+    x = xs[:, :K]
+    w = (0.02 * torch.randn(N, K, generator=g, device=DEV)).to(torch.bfloat16)
+    ref = x.float() @ w.float().t()
+    got = ops.linear_m8(x, w)
+    assert got.shape == (M, N)
+    err = (got.float() - ref).abs().max().item()
+    assert err <= 1e-2 * ref.abs().max().item() + 1e-3, err
+    # into a strided output (a view of a wider buffer)
+    wide = torch.zeros(M, N + 32, device=DEV, dtype=torch.bfloat16)
+    ops.linear_m8(x, w, out=wide[:, 16:16 + N])
+    assert torch.equal(wide[:, 16:16 + N], got) and bool((wide[:, :16] == 0).all())
+    assert _capi.device_error() == 0
+
+
+@pytest.mark.parametrize("M,K,inter", [(8, 4096, 1536), (8, 4096, 12288), (2, 2560, 9728)])
+def test_linear_m8_glu(M, K, inter):
+    """Fused gate/up projection + SwiGLU == silu_mul of the two bf16 projections."""
+    g = torch.Generator(device=DEV).manual_seed(inter)
+    x = torch.randn(M, 1, K, generator=g, device=DEV).to(torch.bfloat16)
+    w = (0.02 * torch.randn(2 * inter, K, generator=g, device=DEV)).to(torch.bfloat16)
+    gu = (x.float() @ w.float().t()).to(torch.bfloat16)
+    ref = torch.nn.functional.silu(gu[..., :inter].float()) * gu[..., inter:].float()
+    got = ops.linear_m8(x, w, glu=True)
+    assert got.shape == (M, 1, inter)
+    err = (got.float() - ref).abs().max().item()
+    assert err <= 2e-2 * ref.abs().max().item() + 1e-3, err
+    assert _capi.device_error() == 0
+
+
+def test_linear_m8_rejects_unsupported_shapes():
+    x = torch.zeros(9, 256, device=DEV, dtype=torch.bfloat16)
+    w = torch.zeros(16, 256, device=DEV, dtype=torch.bfloat16)
+    with pytest.raises(RuntimeError, match="tokens"):
+        ops.linear_m8(x, w)
+    with pytest.raises(RuntimeError, match="multiple"):
+        ops.linear_m8(x[:8, :200], w[:, :200])
