@@ -119,3 +119,24 @@ def test_attention_backend_is_abstract():
     with pytest.raises(TypeError):
         sa.AttentionBackend()
     assert "forward" in sa.AttentionBackend.__abstractmethods__
+
+
+def test_linear_m8_host_validation():
+    """sa_linear_m8 rejects unsupported shapes and layouts before any CUDA call."""
+    lib = _capi.load()
+    P = 1 << 20  # a 16-byte aligned dummy address (never dereferenced: the checks fail first)
+    ok = dict(x=P, M=8, K=4096, xs=4096, w=P, N=768, ws=4096, o=P, os=768, glu=0)
+
+    def call(**kw):
+        a = {**ok, **kw}
+        return lib.sa_linear_m8(a["x"], a["M"], a["K"], a["xs"], a["w"], a["N"], a["ws"], a["o"], a["os"],
+                                a["glu"], None)
+
+    assert call(x=None) == _capi.SA_ERR_INVALID
+    assert call(M=9) == _capi.SA_ERR_UNSUPPORTED and b"tokens" in lib.sa_last_error()
+    assert call(M=0) == _capi.SA_ERR_UNSUPPORTED
+    assert call(K=4000) == _capi.SA_ERR_UNSUPPORTED
+    assert call(N=770) == _capi.SA_ERR_UNSUPPORTED
+    assert call(x=P + 8) == _capi.SA_ERR_INVALID  # rows not on 16-byte boundaries
+    assert call(xs=4100) == _capi.SA_ERR_INVALID
+    assert call(ws=2048) == _capi.SA_ERR_INVALID  # stride shorter than K
